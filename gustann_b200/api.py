@@ -1,0 +1,228 @@
+"""Python mirror of the reference's host API, over the C ABI of libgann.so.
+
+``GustANN`` follows ``gustann::GustANN`` (``src/ssd_search.hpp:29-83``): same
+method names, argument meaning and order. Errors raise :class:`GustANNError`
+(a ``RuntimeError``, as ``CHECK_CUDA`` throws ``std::runtime_error`` in
+``src/common_cuda.cuh:10-17``) carrying the C status code.
+
+The library is loaded from the package directory (``_lib/libgann.so``); there
+is no fallback: if it is missing, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+from .formats import FLOAT, UINT8
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libgann.so")
+
+GANN_OK, GANN_EINVAL, GANN_EIO, GANN_ENOMEM, GANN_ECUDA, GANN_ETIMEDOUT, GANN_EUNSUPPORTED, GANN_ESTATE = range(8)
+STATUS_NAMES = ["OK", "EINVAL", "EIO", "ENOMEM", "ECUDA", "ETIMEDOUT", "EUNSUPPORTED", "ESTATE"]
+
+# Every symbol include/gann.h declares.
+EXPORTS = ["gann_open", "gann_search", "gann_search_device", "gann_close", "gann_last_error",
+           "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample"]
+
+
+class GustANNError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        self.code = code
+        name = STATUS_NAMES[code] if 0 <= code < len(STATUS_NAMES) else str(code)
+        super().__init__(f"GANN_{name}: {msg}")
+
+
+class _Config(C.Structure):
+    _fields_ = [("index_file", C.c_char_p), ("pq_file_prefix", C.c_char_p), ("nav_graph_prefix", C.c_char_p),
+                ("dtype", C.c_int32), ("use_gpu_mem", C.c_int32), ("device", C.c_int32),
+                ("reserved", C.c_int32 * 5)]
+
+
+class _Stats(C.Structure):
+    _fields_ = [("run_time", C.c_double), ("total_time", C.c_double), ("hops", C.c_int64),
+                ("adc_evals", C.c_int64), ("capped_queries", C.c_int64), ("bytes_touched", C.c_int64)]
+
+
+class _Info(C.Structure):
+    _fields_ = [("num_points", C.c_int64), ("dim", C.c_int32), ("max_degree", C.c_int32),
+                ("pq_chunks", C.c_int32), ("dtype", C.c_int32), ("medoid", C.c_int64),
+                ("node_len", C.c_int32), ("nodes_per_page", C.c_int32), ("nav_points", C.c_int32),
+                ("nav_start", C.c_int32), ("device_bytes", C.c_int64)]
+
+
+def _load() -> C.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is not built; run `python -m gustann_b200.build`")
+    lib = C.CDLL(LIB_PATH)
+    vp, i64, i32, fp, ip = C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p
+    lib.gann_open.argtypes = [C.POINTER(_Config), C.POINTER(vp)]
+    lib.gann_search.argtypes = [vp, fp, i64, i32, i32, ip, fp, ip, C.POINTER(_Stats)]
+    lib.gann_search_device.argtypes = [vp, vp, i64, i32, i32, vp, vp, vp, vp, vp]
+    lib.gann_close.argtypes = [vp]
+    lib.gann_last_error.restype = C.c_char_p
+    lib.gann_index_info.argtypes = [vp, C.POINTER(_Info)]
+    lib.gann_probe_lut.argtypes = [vp, fp, i64, fp]
+    lib.gann_probe_entry.argtypes = [vp, fp, i64, ip, ip]
+    lib.gann_pivot_sample.argtypes = [i64, i64, C.c_uint32, ip]
+    for name in EXPORTS:
+        if name != "gann_last_error":
+            getattr(lib, name).restype = C.c_int
+    return lib
+
+
+lib = _load()
+
+
+def _check(rc: int) -> None:
+    if rc != GANN_OK:
+        raise GustANNError(rc, lib.gann_last_error().decode(errors="replace"))
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+@dataclass
+class GustANNConfig:
+    """``gustann::GustANNConfig`` (``src/ssd_search.hpp:18-23``)."""
+
+    index_file: str
+    pq_file_prefix: str
+    nav_graph_prefix: str = ""
+
+
+@dataclass
+class GustANNStats:
+    """``gustann::GustANNStats`` plus the counters of ``gann_stats``."""
+
+    run_time: float = 0.0
+    total_time: float = 0.0
+    hops: int = 0
+    adc_evals: int = 0
+    capped_queries: int = 0
+    bytes_touched: int = 0
+
+
+class GustANN:
+    """Drop-in for ``gustann::GustANN`` on one B200 (``device``)."""
+
+    def __init__(self, data_type: int = FLOAT, device: int = 0):
+        if data_type not in (UINT8, FLOAT):
+            raise GustANNError(GANN_EINVAL, "data type must be UINT8 (0) or FLOAT (1)")
+        self.data_type = data_type
+        self.device = device
+        self._h = None
+        self.dim = 0
+
+    # --------------------------------------------------------------- init
+    def init_pure_mem(self, config: GustANNConfig, use_gpu_mem: bool) -> None:
+        """``GustANN::init_pure_mem`` (``src/ssd_search.cu:108-112``)."""
+        self.close()
+        cfg = _Config(config.index_file.encode(), config.pq_file_prefix.encode(),
+                      (config.nav_graph_prefix or "").encode(), self.data_type, int(bool(use_gpu_mem)),
+                      self.device)
+        h = C.c_void_p()
+        _check(lib.gann_open(C.byref(cfg), C.byref(h)))
+        self._h = h
+        self.dim = self.info()["dim"]
+
+    def init_hybrid(self, *args, **kwargs) -> None:
+        """The SSD-tiered executor is not part of this build."""
+        raise GustANNError(GANN_EUNSUPPORTED, "init_hybrid: SSD-hybrid search is not provided by this build")
+
+    def init_bam(self, *args, **kwargs) -> None:
+        raise GustANNError(GANN_EUNSUPPORTED, "init_bam: BaM search is not provided by this build")
+
+    # ------------------------------------------------------------- search
+    def search(self, qdata: np.ndarray, num_queries: int, topk: int, ef_search: int, nns: np.ndarray,
+               distances: np.ndarray, found_cnt: np.ndarray, stats: GustANNStats | None = None) -> None:
+        """``GustANN::search`` (``src/ssd_search.cu:114-140``): fills ``nns``,
+        ``distances`` (squared L2) and ``found_cnt`` in place."""
+        self._need()
+        q = np.ascontiguousarray(qdata, dtype=np.float32)
+        if q.size < num_queries * self.dim:
+            raise GustANNError(GANN_EINVAL, "search: qdata holds fewer than num_queries rows")
+        for arr, dt, n in ((nns, np.int32, num_queries * topk), (distances, np.float32, num_queries * topk),
+                           (found_cnt, np.int32, num_queries)):
+            if arr.dtype != dt or not arr.flags.c_contiguous or arr.size < n:
+                raise GustANNError(GANN_EINVAL, "search: output arrays must be contiguous int32/float32 of the right size")
+        st = _Stats()
+        _check(lib.gann_search(self._h, _ptr(q), num_queries, topk, ef_search, _ptr(nns), _ptr(distances),
+                               _ptr(found_cnt), C.byref(st)))
+        if stats is not None:
+            for f, _ in _Stats._fields_:
+                setattr(stats, f, getattr(st, f))
+
+    def query(self, qdata: np.ndarray, topk: int, ef_search: int, stats: GustANNStats | None = None):
+        """Convenience form of :meth:`search` returning ``(nns, distances, found_cnt)``."""
+        q = np.ascontiguousarray(qdata, dtype=np.float32).reshape(-1, self.dim if self.dim else qdata.shape[-1])
+        nq = q.shape[0]
+        nns = np.zeros((nq, topk), np.int32)
+        dist = np.zeros((nq, topk), np.float32)
+        found = np.zeros(nq, np.int32)
+        self.search(q, nq, topk, ef_search, nns, dist, found, stats)
+        return nns, dist, found
+
+    def search_device(self, d_queries: int, num_queries: int, topk: int, ef_search: int, d_nns: int,
+                      d_distances: int, d_found_cnt: int, d_hops: int = 0, stream: int = 0) -> None:
+        """Device-pointer search (``gann_search_device``); pointers are ints
+        (e.g. ``tensor.data_ptr()``), ``stream`` a ``cudaStream_t`` handle."""
+        self._need()
+        _check(lib.gann_search_device(self._h, d_queries, num_queries, topk, ef_search, d_nns, d_distances,
+                                      d_found_cnt, d_hops or None, stream or None))
+
+    # ------------------------------------------------------------- probes
+    def probe_lut(self, qdata: np.ndarray) -> np.ndarray:
+        self._need()
+        q = np.ascontiguousarray(qdata, dtype=np.float32).reshape(-1, self.dim)
+        m = self.info()["pq_chunks"]
+        out = np.zeros((q.shape[0], m, 256), np.float32)
+        _check(lib.gann_probe_lut(self._h, _ptr(q), q.shape[0], _ptr(out)))
+        return out
+
+    def probe_entry(self, qdata: np.ndarray):
+        self._need()
+        q = np.ascontiguousarray(qdata, dtype=np.float32).reshape(-1, self.dim)
+        s = np.zeros(q.shape[0], np.int32)
+        e = np.zeros(q.shape[0], np.int32)
+        _check(lib.gann_probe_entry(self._h, _ptr(q), q.shape[0], _ptr(s), _ptr(e)))
+        return s, e
+
+    def info(self) -> dict:
+        self._need()
+        inf = _Info()
+        _check(lib.gann_index_info(self._h, C.byref(inf)))
+        return {f: getattr(inf, f) for f, _ in _Info._fields_}
+
+    # ---------------------------------------------------------- lifetime
+    def close(self) -> None:
+        if self._h is not None:
+            lib.gann_close(self._h)
+            self._h = None
+
+    def _need(self) -> None:
+        if self._h is None:
+            raise GustANNError(GANN_ESTATE, "GustANN used before init_pure_mem")
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+def pivot_sample(n: int, s: int, seed: int = 114514) -> np.ndarray:
+    """Sorted pivot-graph sample ids (``bin/gen_small_file.cpp:18-40`` sampling)."""
+    out = np.zeros(s, np.int32)
+    _check(lib.gann_pivot_sample(n, s, seed, _ptr(out)))
+    return out

@@ -1,0 +1,447 @@
+// C ABI of libgann.so: index load onto one B200, search orchestration, stage
+// probes. See include/gann.h for the contract of every entry point.
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <numeric>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "gann_internal.hpp"
+
+using gann::DeviceIndex;
+using gann::HostIndex;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int set_error(int code, const std::string& m) {
+  g_last_error = m;
+  return code;
+}
+
+#define GANN_CUDA(call)                                                                          \
+  do {                                                                                           \
+    cudaError_t e_ = (call);                                                                     \
+    if (e_ != cudaSuccess)                                                                       \
+      return set_error(e_ == cudaErrorMemoryAllocation ? GANN_ENOMEM : GANN_ECUDA,               \
+                       std::string("CUDA error: ") + cudaGetErrorString(e_) + " (" #call ")"); \
+  } while (0)
+
+template <typename T>
+int dev_upload(T*& dst, const T* src, size_t count, int64_t& bytes) {
+  if (count == 0) return GANN_OK;
+  GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&dst), sizeof(T) * count));
+  bytes += static_cast<int64_t>(sizeof(T) * count);
+  GANN_CUDA(cudaMemcpy(dst, src, sizeof(T) * count, cudaMemcpyHostToDevice));
+  return GANN_OK;
+}
+
+}  // namespace
+
+struct gann_handle {
+  int device = 0;
+  int dtype = GANN_FLOAT;
+  bool host_records = false;
+  bool cuda_ready = false;           // a CUDA context exists for `device`
+  HostIndex hi;
+  DeviceIndex ix;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  // owned allocations
+  uint8_t* vecs = nullptr;
+  uint32_t* adj = nullptr;
+  uint8_t* codes = nullptr;
+  float* pivots_t = nullptr;
+  float* centroid = nullptr;
+  int32_t* chunk_off = nullptr;
+  uint8_t* nav_vecs = nullptr;
+  int32_t* nav_adj = nullptr;
+  int32_t* nav_map = nullptr;
+  int32_t* counter = nullptr;        // [0]: work counter, [1..2]: error counts
+  int64_t device_bytes = 0;
+  // reusable buffers of gann_search
+  int64_t cap_q = 0, cap_out = 0;
+  float* d_q = nullptr;
+  int32_t* d_nns = nullptr;
+  float* d_dist = nullptr;
+  int32_t* d_found = nullptr;
+  uint32_t* d_hops = nullptr;
+  uint32_t* d_adc = nullptr;
+
+  void release() {
+    if (!cuda_ready) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    if (host_records) {
+      if (vecs) cudaFreeHost(vecs);
+      if (adj) cudaFreeHost(adj);
+    } else {
+      if (vecs) cudaFree(vecs);
+      if (adj) cudaFree(adj);
+    }
+    for (void* p : {static_cast<void*>(codes), static_cast<void*>(pivots_t), static_cast<void*>(centroid),
+                    static_cast<void*>(chunk_off), static_cast<void*>(nav_vecs), static_cast<void*>(nav_adj),
+                    static_cast<void*>(nav_map), static_cast<void*>(counter), static_cast<void*>(d_q),
+                    static_cast<void*>(d_nns), static_cast<void*>(d_dist), static_cast<void*>(d_found),
+                    static_cast<void*>(d_hops), static_cast<void*>(d_adc)})
+      if (p) cudaFree(p);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (stream) cudaStreamDestroy(stream);
+    vecs = nullptr;
+    adj = nullptr;
+    cudaSetDevice(prev);
+  }
+};
+
+namespace {
+
+int load_records(gann_handle* h, const std::string& path) {
+  HostIndex& hi = h->hi;
+  const int64_t n = hi.num_points;
+  const int64_t vs = gann::round_up(hi.dim, 32) * hi.elem;
+  const int32_t as = static_cast<int32_t>(gann::round_up(hi.max_m0, 4));
+  const size_t vbytes = static_cast<size_t>(n) * vs, abytes = static_cast<size_t>(n) * as * 4;
+  std::string msg;
+  if (h->host_records) {
+    // records stay in pinned host memory and are read by the kernel through
+    // the unified address space (the reference's search_graph_kernel_dram mode)
+    GANN_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->vecs), vbytes, cudaHostAllocMapped | cudaHostAllocPortable));
+    GANN_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->adj), abytes, cudaHostAllocMapped | cudaHostAllocPortable));
+    const int64_t blk = 1 << 20;
+    for (int64_t r = 0; r < n; r += blk) {
+      const int64_t c = std::min(blk, n - r);
+      int rc = gann::relayout_records(path, hi, r, c, h->vecs + r * vs, vs, h->adj + r * as, as, msg);
+      if (rc) return set_error(rc, msg);
+    }
+  } else {
+    GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->vecs), vbytes));
+    GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->adj), abytes));
+    h->device_bytes += static_cast<int64_t>(vbytes + abytes);
+    const int64_t blk = 1 << 20;
+    std::vector<uint8_t> sv(static_cast<size_t>(std::min(blk, n)) * vs);
+    std::vector<uint32_t> sa(static_cast<size_t>(std::min(blk, n)) * as);
+    for (int64_t r = 0; r < n; r += blk) {
+      const int64_t c = std::min(blk, n - r);
+      int rc = gann::relayout_records(path, hi, r, c, sv.data(), vs, sa.data(), as, msg);
+      if (rc) return set_error(rc, msg);
+      GANN_CUDA(cudaMemcpy(h->vecs + r * vs, sv.data(), static_cast<size_t>(c) * vs, cudaMemcpyHostToDevice));
+      GANN_CUDA(cudaMemcpy(h->adj + r * as, sa.data(), static_cast<size_t>(c) * as * 4, cudaMemcpyHostToDevice));
+    }
+  }
+  h->ix.vecs = h->vecs;
+  h->ix.adj = h->adj;
+  h->ix.vec_stride = vs;
+  h->ix.adj_stride = as;
+  return GANN_OK;
+}
+
+int open_impl(const gann_config* cfg, gann_handle* h) {
+  if (!cfg || !cfg->index_file || !cfg->pq_file_prefix)
+    return set_error(GANN_EINVAL, "gann_open: index_file and pq_file_prefix are required");
+  if (cfg->dtype != GANN_UINT8 && cfg->dtype != GANN_FLOAT)
+    return set_error(GANN_EINVAL, "gann_open: dtype must be GANN_UINT8 or GANN_FLOAT");
+  h->device = cfg->device;
+  h->dtype = cfg->dtype;
+  h->host_records = cfg->use_gpu_mem == 0;
+
+  // parse and validate every file before touching the GPU
+  HostIndex& hi = h->hi;
+  hi.dtype = cfg->dtype;
+  const int elem = cfg->dtype == GANN_UINT8 ? 1 : 4;
+  std::string msg;
+  int rc = gann::load_disk_header(cfg->index_file, elem, hi, msg);
+  if (rc) return set_error(rc, msg);
+  std::vector<uint8_t> codes;
+  int64_t rows = 0;
+  rc = gann::load_pq(cfg->pq_file_prefix, hi, codes, rows, msg);
+  if (rc) return set_error(rc, msg);
+  if (cfg->nav_graph_prefix && cfg->nav_graph_prefix[0]) {
+    rc = gann::load_nav(cfg->nav_graph_prefix, hi, msg);
+    if (rc) return set_error(rc, msg);
+  }
+
+  int ndev = 0;
+  GANN_CUDA(cudaGetDeviceCount(&ndev));
+  if (cfg->device < 0 || cfg->device >= ndev) return set_error(GANN_EINVAL, "gann_open: no such CUDA device");
+  GANN_CUDA(cudaSetDevice(h->device));
+  h->cuda_ready = true;
+  GANN_CUDA(cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, h->device));
+  GANN_CUDA(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+  GANN_CUDA(cudaEventCreate(&h->ev0));
+  GANN_CUDA(cudaEventCreate(&h->ev1));
+
+  DeviceIndex& ix = h->ix;
+  ix.n = hi.num_points;
+  ix.dim = static_cast<int32_t>(hi.dim);
+  ix.degree = static_cast<int32_t>(hi.max_m0);
+  ix.chunks = hi.num_chunks;
+  ix.code_stride = static_cast<int32_t>(gann::round_up(hi.num_chunks, 16));
+  ix.medoid = hi.medoid;
+  if ((rc = dev_upload(h->codes, codes.data(), codes.size(), h->device_bytes))) return rc;
+  codes.clear();
+  codes.shrink_to_fit();
+  if ((rc = dev_upload(h->pivots_t, hi.pivots_t.data(), hi.pivots_t.size(), h->device_bytes))) return rc;
+  if ((rc = dev_upload(h->centroid, hi.centroid.data(), hi.centroid.size(), h->device_bytes))) return rc;
+  if ((rc = dev_upload(h->chunk_off, hi.chunk_offsets.data(), hi.chunk_offsets.size(), h->device_bytes))) return rc;
+  ix.codes = h->codes;
+  ix.pivots_t = h->pivots_t;
+  ix.centroid = h->centroid;
+  ix.chunk_off = h->chunk_off;
+  if (hi.has_nav) {
+    if ((rc = dev_upload(h->nav_vecs, hi.nav_vecs.data(), hi.nav_vecs.size(), h->device_bytes))) return rc;
+    if ((rc = dev_upload(h->nav_adj, hi.nav_adj.data(), hi.nav_adj.size(), h->device_bytes))) return rc;
+    if ((rc = dev_upload(h->nav_map, hi.nav_map.data(), hi.nav_map.size(), h->device_bytes))) return rc;
+    ix.nav_vecs = h->nav_vecs;
+    ix.nav_adj = h->nav_adj;
+    ix.nav_map = h->nav_map;
+    ix.nav_stride = gann::round_up(hi.dim, 32) * hi.elem;
+    ix.nav_row = hi.nav_max_m;
+    ix.nav_start = hi.nav_start;
+    ix.nav_points = hi.nav_points;
+    ix.has_nav = 1;
+    hi.nav_vecs.clear();
+    hi.nav_vecs.shrink_to_fit();
+  }
+  GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->counter), 4 * sizeof(int32_t)));
+  if ((rc = load_records(h, cfg->index_file))) return rc;
+  return GANN_OK;
+}
+
+int check_search_args(gann_handle* h, int64_t nq, int32_t topk, int32_t ef) {
+  if (!h) return set_error(GANN_EINVAL, "search: null handle");
+  if (nq < 0 || nq >= (int64_t(1) << 31) - (int64_t(1) << 24))
+    return set_error(GANN_EINVAL, "search: query count out of range");
+  if (topk < 1 || topk > ef) return set_error(GANN_EINVAL, "search: need 1 <= topk <= ef_search");
+  if (ef > gann::search_max_ef())
+    return set_error(GANN_EUNSUPPORTED, "search: ef_search above " + std::to_string(gann::search_max_ef()));
+  int per_sm_smem = 0;
+  cudaDeviceGetAttribute(&per_sm_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, h->device);
+  if (gann::search_smem_bytes(h->ix, topk, ef) > static_cast<size_t>(per_sm_smem))
+    return set_error(GANN_EUNSUPPORTED, "search: per-query working set exceeds shared memory");
+  return GANN_OK;
+}
+
+gann::SearchArgs make_args(gann_handle* h, const float* q, int64_t nq, int32_t topk, int32_t ef,
+                           int32_t* nns, float* dist, int32_t* found, uint32_t* hops, uint32_t* adc) {
+  gann::SearchArgs a;
+  a.q = q;
+  a.nq = nq;
+  a.topk = topk;
+  a.ef = ef;
+  // generous bounds: a best-first search expands about ef..2*ef nodes
+  a.max_hops = std::max(1 << 14, 64 * ef);
+  a.nav_max_hops = 1 << 20;
+  a.nns = nns;
+  a.dist = dist;
+  a.found = found;
+  a.hops = hops;
+  a.adc = adc;
+  a.qcounter = h->counter;
+  a.err = h->counter + 1;
+  return a;
+}
+
+template <typename T>
+int grow(T*& p, int64_t count) {
+  if (p) cudaFree(p);
+  p = nullptr;
+  GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&p), sizeof(T) * std::max<int64_t>(count, 1)));
+  return GANN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gann_open(const gann_config* cfg, gann_handle** out) {
+  if (!out) return set_error(GANN_EINVAL, "gann_open: out is NULL");
+  *out = nullptr;
+  gann_handle* h = new (std::nothrow) gann_handle();
+  if (!h) return set_error(GANN_ENOMEM, "gann_open: out of host memory");
+  int rc;
+  try {
+    rc = open_impl(cfg, h);
+  } catch (const std::bad_alloc&) {
+    rc = set_error(GANN_ENOMEM, "gann_open: out of host memory");
+  }
+  if (rc != GANN_OK) {
+    h->release();
+    delete h;
+    return rc;
+  }
+  *out = h;
+  return GANN_OK;
+}
+
+int gann_close(gann_handle* h) {
+  if (!h) return GANN_OK;
+  h->release();
+  delete h;
+  return GANN_OK;
+}
+
+const char* gann_last_error(void) { return g_last_error.c_str(); }
+
+int gann_index_info(const gann_handle* h, gann_info* out) {
+  if (!h || !out) return set_error(GANN_EINVAL, "gann_index_info: null argument");
+  std::memset(out, 0, sizeof(*out));
+  out->num_points = h->hi.num_points;
+  out->dim = static_cast<int32_t>(h->hi.dim);
+  out->max_degree = static_cast<int32_t>(h->hi.max_m0);
+  out->pq_chunks = h->hi.num_chunks;
+  out->dtype = h->dtype;
+  out->medoid = h->hi.medoid;
+  out->node_len = static_cast<int32_t>(h->hi.max_node_len);
+  out->nodes_per_page = static_cast<int32_t>(h->hi.nodes_per_page);
+  out->nav_points = static_cast<int32_t>(h->hi.nav_points);
+  out->nav_start = h->hi.nav_start;
+  out->device_bytes = h->device_bytes;
+  return GANN_OK;
+}
+
+int gann_search_device(gann_handle* h, const float* d_queries, int64_t nq, int32_t topk, int32_t ef_search,
+                       int32_t* d_nns, float* d_distances, int32_t* d_found_cnt, uint32_t* d_hops_out,
+                       void* stream) {
+  int rc = check_search_args(h, nq, topk, ef_search);
+  if (rc) return rc;
+  if (nq == 0) return GANN_OK;
+  if (!d_queries || !d_nns || !d_distances || !d_found_cnt)
+    return set_error(GANN_EINVAL, "gann_search_device: null buffer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GANN_CUDA(cudaSetDevice(h->device));
+  GANN_CUDA(cudaMemsetAsync(h->counter, 0, 4 * sizeof(int32_t), st));
+  gann::SearchArgs a = make_args(h, d_queries, nq, topk, ef_search, d_nns, d_distances, d_found_cnt,
+                                 d_hops_out, nullptr);
+  GANN_CUDA(gann::launch_search(h->ix, a, h->dtype, h->sm_count, st));
+  return GANN_OK;
+}
+
+int gann_search(gann_handle* h, const float* queries, int64_t nq, int32_t topk, int32_t ef_search,
+                int32_t* nns, float* distances, int32_t* found_cnt, gann_stats* stats) {
+  const auto t0 = std::chrono::steady_clock::now();
+  int rc = check_search_args(h, nq, topk, ef_search);
+  if (rc) return rc;
+  if (stats) std::memset(stats, 0, sizeof(*stats));
+  if (nq == 0) return GANN_OK;
+  if (!queries || !nns || !distances || !found_cnt) return set_error(GANN_EINVAL, "gann_search: null buffer");
+  GANN_CUDA(cudaSetDevice(h->device));
+  const int64_t dim = h->hi.dim;
+  if (nq * dim > h->cap_q) {
+    if ((rc = grow(h->d_q, nq * dim))) return rc;
+    h->cap_q = nq * dim;
+  }
+  if (nq * topk > h->cap_out || nq > h->cap_out) {
+    const int64_t c = std::max(nq * topk, nq);
+    if ((rc = grow(h->d_nns, c)) || (rc = grow(h->d_dist, c)) || (rc = grow(h->d_found, c)) ||
+        (rc = grow(h->d_hops, c)) || (rc = grow(h->d_adc, c)))
+      return rc;
+    h->cap_out = c;
+  }
+  cudaStream_t st = h->stream;
+  GANN_CUDA(cudaMemcpyAsync(h->d_q, queries, sizeof(float) * nq * dim, cudaMemcpyHostToDevice, st));
+  GANN_CUDA(cudaMemsetAsync(h->counter, 0, 4 * sizeof(int32_t), st));
+  gann::SearchArgs a = make_args(h, h->d_q, nq, topk, ef_search, h->d_nns, h->d_dist, h->d_found, h->d_hops,
+                                 h->d_adc);
+  GANN_CUDA(cudaEventRecord(h->ev0, st));
+  GANN_CUDA(gann::launch_search(h->ix, a, h->dtype, h->sm_count, st));
+  GANN_CUDA(cudaEventRecord(h->ev1, st));
+  GANN_CUDA(cudaMemcpyAsync(nns, h->d_nns, sizeof(int32_t) * nq * topk, cudaMemcpyDeviceToHost, st));
+  GANN_CUDA(cudaMemcpyAsync(distances, h->d_dist, sizeof(float) * nq * topk, cudaMemcpyDeviceToHost, st));
+  GANN_CUDA(cudaMemcpyAsync(found_cnt, h->d_found, sizeof(int32_t) * nq, cudaMemcpyDeviceToHost, st));
+  std::vector<uint32_t> hops, adc;
+  int32_t errs[4] = {0, 0, 0, 0};
+  if (stats) {
+    hops.resize(nq);
+    adc.resize(nq);
+    GANN_CUDA(cudaMemcpyAsync(hops.data(), h->d_hops, sizeof(uint32_t) * nq, cudaMemcpyDeviceToHost, st));
+    GANN_CUDA(cudaMemcpyAsync(adc.data(), h->d_adc, sizeof(uint32_t) * nq, cudaMemcpyDeviceToHost, st));
+    GANN_CUDA(cudaMemcpyAsync(errs, h->counter, sizeof(errs), cudaMemcpyDeviceToHost, st));
+  }
+  GANN_CUDA(cudaStreamSynchronize(st));
+  if (stats) {
+    float ms = 0.f;
+    GANN_CUDA(cudaEventElapsedTime(&ms, h->ev0, h->ev1));
+    stats->run_time = ms * 1e-3;
+    int64_t sh = 0, sa = 0;
+    for (int64_t i = 0; i < nq; ++i) {
+      sh += hops[i];
+      sa += adc[i];
+    }
+    stats->hops = sh;
+    stats->adc_evals = sa;
+    stats->capped_queries = errs[1];
+    // algorithmic bytes: query + per hop one record + one PQ code row per
+    // evaluated neighbour + the top-k written back
+    stats->bytes_touched = nq * dim * h->hi.elem + sh * h->hi.max_node_len + sa * h->hi.num_chunks +
+                           nq * topk * 8;
+    stats->total_time = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  }
+  return GANN_OK;
+}
+
+int gann_probe_lut(gann_handle* h, const float* queries, int64_t nq, float* luts) {
+  if (!h || nq < 0 || (nq > 0 && (!queries || !luts))) return set_error(GANN_EINVAL, "gann_probe_lut: bad argument");
+  if (nq == 0) return GANN_OK;
+  GANN_CUDA(cudaSetDevice(h->device));
+  float *dq = nullptr, *dl = nullptr;
+  const size_t lut_n = static_cast<size_t>(nq) * h->hi.num_chunks * gann::kPivots;
+  GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&dq), sizeof(float) * nq * h->hi.dim));
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&dl), sizeof(float) * lut_n);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dq, queries, sizeof(float) * nq * h->hi.dim, cudaMemcpyHostToDevice, h->stream);
+  if (e == cudaSuccess) e = gann::launch_probe_lut(h->ix, dq, nq, dl, h->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(luts, dl, sizeof(float) * lut_n, cudaMemcpyDeviceToHost, h->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+  cudaFree(dq);
+  cudaFree(dl);
+  if (e != cudaSuccess) return set_error(GANN_ECUDA, std::string("gann_probe_lut: ") + cudaGetErrorString(e));
+  return GANN_OK;
+}
+
+int gann_probe_entry(gann_handle* h, const float* queries, int64_t nq, int32_t* sample_idx, int32_t* entry_ids) {
+  if (!h || nq < 0 || (nq > 0 && (!queries || !sample_idx || !entry_ids)))
+    return set_error(GANN_EINVAL, "gann_probe_entry: bad argument");
+  if (!h->ix.has_nav) return set_error(GANN_ESTATE, "gann_probe_entry: index opened without a nav graph");
+  if (nq == 0) return GANN_OK;
+  GANN_CUDA(cudaSetDevice(h->device));
+  float* dq = nullptr;
+  int32_t* dbuf = nullptr;
+  GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&dq), sizeof(float) * nq * h->hi.dim));
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&dbuf), sizeof(int32_t) * (2 * nq + 1));
+  if (e == cudaSuccess) e = cudaMemsetAsync(dbuf, 0, sizeof(int32_t) * (2 * nq + 1), h->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dq, queries, sizeof(float) * nq * h->hi.dim, cudaMemcpyHostToDevice, h->stream);
+  if (e == cudaSuccess) e = gann::launch_probe_entry(h->ix, dq, nq, h->dtype, dbuf, dbuf + nq, dbuf + 2 * nq, h->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(sample_idx, dbuf, sizeof(int32_t) * nq, cudaMemcpyDeviceToHost, h->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(entry_ids, dbuf + nq, sizeof(int32_t) * nq, cudaMemcpyDeviceToHost, h->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+  cudaFree(dq);
+  cudaFree(dbuf);
+  if (e != cudaSuccess) return set_error(GANN_ECUDA, std::string("gann_probe_entry: ") + cudaGetErrorString(e));
+  return GANN_OK;
+}
+
+int gann_pivot_sample(int64_t n, int64_t s, uint32_t seed, int32_t* out) {
+  if (n <= 0 || n >= (int64_t(1) << 31) || s < 0 || s > n || (s > 0 && !out))
+    return set_error(GANN_EINVAL, "gann_pivot_sample: need 0 <= s <= n < 2^31");
+  try {
+    std::vector<int> v(static_cast<size_t>(n));
+    std::iota(v.begin(), v.end(), 0);
+    std::mt19937 gen(seed);
+    std::shuffle(v.begin(), v.end(), gen);
+    v.resize(static_cast<size_t>(s));
+    std::sort(v.begin(), v.end());
+    std::copy(v.begin(), v.end(), out);
+  } catch (const std::bad_alloc&) {
+    return set_error(GANN_ENOMEM, "gann_pivot_sample: out of host memory");
+  }
+  return GANN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,105 @@
+// Internal structures shared by the loader, the C ABI and the kernels.
+#pragma once
+
+#include <cstdint>
+#include <cstddef>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "gann.h"
+
+namespace gann {
+
+constexpr int kWarp = 32;
+constexpr int kPivots = 256;            // PQSearchData::num_pivots (src/pq_search.hpp:12)
+constexpr uint32_t kPadId = 0xffffffffu;
+constexpr uint32_t kVisited = 0x80000000u;
+constexpr int kNavSlots = 32;           // nav pool: 4 best + 28 neighbour slots
+constexpr int kNavBest = 4;             // src/impl/nav.cuh:11
+constexpr int kNavNbr = 28;             // src/impl/nav.cuh:12
+constexpr int kPageSize = 4096;
+
+// Host-side copy of everything parsed from the three index inputs.
+struct HostIndex {
+  int dtype = GANN_FLOAT;
+  int elem = 4;
+  // disk index header (src/layout.cpp:25-54)
+  int64_t num_points = 0, dim = 0, medoid = 0;
+  int64_t max_node_len = 0, nodes_per_page = 0, max_m0 = 0, data_size = 0, num_pages = 0;
+  // PQ (src/pq_search.cu:56-121)
+  int num_chunks = 0;
+  std::vector<float> pivots_t;          // [dim x 256], transposed like the reference
+  std::vector<float> centroid;          // [dim]
+  std::vector<int32_t> chunk_offsets;   // [M+1]
+  // nav graph (src/nav_graph.cu:41-100)
+  bool has_nav = false;
+  int64_t nav_points = 0;
+  int32_t nav_max_m = 0, nav_start = 0;
+  std::vector<uint8_t> nav_vecs;        // [S x nav_stride] bytes
+  std::vector<int32_t> nav_adj;         // [S x nav_max_m] + 32 tail, -1 padded
+  std::vector<int32_t> nav_map;         // [S]
+};
+
+// Device layout: records split into aligned vector rows and adjacency rows.
+struct DeviceIndex {
+  const uint8_t* vecs = nullptr;     // [N x vec_stride]
+  const uint32_t* adj = nullptr;     // [N x adj_stride] u32, kPadId after deg
+  const uint8_t* codes = nullptr;    // [N x code_stride]
+  const float* pivots_t = nullptr;   // [D x 256]
+  const float* centroid = nullptr;   // [D]
+  const int32_t* chunk_off = nullptr;// [M+1]
+  const uint8_t* nav_vecs = nullptr; // [S x nav_stride]
+  const int32_t* nav_adj = nullptr;  // [S x nav_row] + 32 tail, -1 padded
+  const int32_t* nav_map = nullptr;  // [S]
+  int64_t n = 0;
+  int32_t dim = 0, degree = 0, chunks = 0;
+  int64_t vec_stride = 0;            // bytes, multiple of 32 elements
+  int32_t adj_stride = 0;            // u32 words
+  int32_t code_stride = 0;           // bytes, multiple of 16
+  int64_t nav_stride = 0;            // bytes
+  int32_t nav_start = 0, has_nav = 0, nav_row = 0;
+  int64_t nav_points = 0;
+  int64_t medoid = 0;
+};
+
+struct SearchArgs {
+  const float* q = nullptr;
+  int64_t nq = 0;
+  int32_t topk = 0, ef = 0;
+  int32_t max_hops = 0, nav_max_hops = 0;
+  int32_t* nns = nullptr;
+  float* dist = nullptr;
+  int32_t* found = nullptr;
+  uint32_t* hops = nullptr;        // nullable
+  uint32_t* adc = nullptr;         // nullable
+  int32_t* qcounter = nullptr;     // work counter (zeroed before launch)
+  int32_t* err = nullptr;          // [2]: capped queries, capped nav searches
+};
+
+// Kernel launchers (gann_search.cu)
+cudaError_t launch_search(const DeviceIndex& ix, const SearchArgs& a, int dtype,
+                          int sm_count, cudaStream_t st);
+cudaError_t launch_probe_lut(const DeviceIndex& ix, const float* d_q, int64_t nq,
+                             float* d_lut, cudaStream_t st);
+cudaError_t launch_probe_entry(const DeviceIndex& ix, const float* d_q, int64_t nq,
+                               int dtype, int32_t* d_sample, int32_t* d_entry,
+                               int32_t* d_err, cudaStream_t st);
+size_t search_smem_bytes(const DeviceIndex& ix, int topk, int ef);
+int search_max_ef();
+
+// Loader (gann_loader.cpp). Return GANN_* and fill `msg` on error.
+int load_disk_header(const std::string& path, int elem, HostIndex& hi, std::string& msg);
+int load_pq(const std::string& prefix, HostIndex& hi, std::vector<uint8_t>& codes,
+            int64_t& code_rows, std::string& msg);
+int load_nav(const std::string& dir, HostIndex& hi, std::string& msg);
+// Read records [first, first+count) of the disk index and split them into
+// vector rows and padded adjacency rows; validates degrees and ids.
+int relayout_records(const std::string& path, const HostIndex& hi, int64_t first, int64_t count,
+                     uint8_t* vec_out, int64_t vec_stride, uint32_t* adj_out, int32_t adj_stride,
+                     std::string& msg);
+
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+}  // namespace gann

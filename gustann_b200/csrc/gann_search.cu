@@ -1,0 +1,647 @@
+// Fused search kernel for sm_100a: one warp owns one query at a time and runs
+// entry selection on the pivot graph, the ADC table build, the best-first
+// traversal and the exact re-rank without leaving the SM.
+//
+// Results equal the reference's (src/impl/pure_mem.cuh:243-432 with
+// src/impl/nav.cuh:13-135 and src/impl/pq.cuh:8-59) on the same inputs. The
+// floating-point operations that decide the traversal are issued in the
+// reference's order:
+//   * ADC table entry: per chunk, dims ascending, acc = fma(d, d, acc) from 0
+//     with d = (q_i - centroid_i) - pivot_ji          (src/impl/pq.cuh:22-43)
+//   * ADC distance: sequential fp32 adds over chunks 0..M-1
+//                                                     (src/impl/pure_mem.cuh:303-308)
+//   * exact distance: lane-strided fma partial sums, then the shfl_down tree
+//     16/8/4/2/1 (src/impl/util.cuh:26-46), on q'' = (q - c) + c for the
+//     traversal re-rank and on q for the pivot graph.
+// Candidate order is the total order (distance, id & 0x7fffffff)
+// (src/impl/util.cuh:166-178); the pool keeps the first `ef` distinct entries
+// of merge(pool, neighbours) with the pool copy first on equal keys, which is
+// what the reference's merge + 2L cut + dedup produce
+// (src/impl/pure_mem.cuh:350-419).
+#include <cstdint>
+#include <climits>
+
+#include "gann_internal.hpp"
+
+namespace gann {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// Distances become the high word of a 64-bit sort key. Adding +0.0f folds -0
+// into +0, because the reference compares distances with < and ==.
+__device__ __forceinline__ uint32_t ord_f32(float f) {
+  uint32_t b = __float_as_uint(__fadd_rn(f, 0.0f));
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Pool / candidate key: [ord(dist) : 32][id : 31][unvisited : 1]. Comparing
+// key >> 1 compares (dist, id); a visited pool copy sorts before an unvisited
+// copy of the same node.
+__device__ __forceinline__ uint64_t make_key(float d, uint32_t id) {
+  return (static_cast<uint64_t>(ord_f32(d)) << 32) | (static_cast<uint64_t>(id) << 1) | 1ull;
+}
+
+template <typename T>
+__device__ __forceinline__ void load32(const T* __restrict__ p, float (&v)[32]);
+
+template <>
+__device__ __forceinline__ void load32<uint8_t>(const uint8_t* __restrict__ p, float (&v)[32]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+  uint4 a = __ldg(q), b = __ldg(q + 1);
+  uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = static_cast<float>((w[i >> 2] >> (8 * (i & 3))) & 0xffu);
+}
+
+template <>
+__device__ __forceinline__ void load32<float>(const float* __restrict__ p, float (&v)[32]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float4 t = __ldg(q + i);
+    v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+  }
+}
+
+// Exact squared L2 with the reference's warp order: lane l sums dims l, l+32, ...
+// with fma, then the shfl_down tree (src/impl/util.cuh:26-46). All lanes get
+// lane 0's value.
+template <typename T>
+__device__ __forceinline__ float warp_sqdist(const float* __restrict__ qv, const T* __restrict__ x,
+                                             int dim, int lane) {
+  float acc = 0.f;
+  for (int i = lane; i < dim; i += kWarp) {
+    float d = __fsub_rn(qv[i], static_cast<float>(x[i]));
+    acc = __fmaf_rn(d, d, acc);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, off));
+  return __shfl_sync(kFull, acc, 0);
+}
+
+// The same value computed by ONE lane for a whole vector: the 32 lane partials
+// live in registers and the shfl_down tree is replayed (lane 0's sum at every
+// level), so 28 pivot-graph neighbours are measured at once, one per lane.
+template <typename T>
+__device__ __forceinline__ float lane_sqdist(const float* __restrict__ qv, const T* __restrict__ x,
+                                             int dim) {
+  float p[32];
+#pragma unroll
+  for (int m = 0; m < 32; ++m) p[m] = 0.f;
+  for (int base = 0; base < dim; base += 32) {
+    float xv[32];
+    load32<T>(x + base, xv);
+#pragma unroll
+    for (int m = 0; m < 32; ++m) {
+      if (base + m < dim) {
+        float d = __fsub_rn(qv[base + m], xv[m]);
+        p[m] = __fmaf_rn(d, d, p[m]);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+    for (int m = 0; m < off; ++m) p[m] = __fadd_rn(p[m], p[m + off]);
+  }
+  return p[0];
+}
+
+// Greedy entry search on the pivot graph (src/impl/nav.cuh:13-135), lane = slot.
+// Slots [0,4) hold the best entries, [4,32) the neighbours of the last expanded
+// node; slots past the neighbour count keep stale entries, as in the reference.
+// Returns the sample index of slot 0.
+template <typename T>
+__device__ int nav_search(const DeviceIndex& ix, const float* __restrict__ qs, int lane,
+                          int max_hops, bool& capped) {
+  const T* nv = reinterpret_cast<const T*>(ix.nav_vecs);
+  const size_t rs = static_cast<size_t>(ix.nav_stride) / sizeof(T);
+  const int start = ix.nav_start;
+  const float d0 = warp_sqdist<T>(qs, nv + static_cast<size_t>(start) * rs, ix.dim, lane);
+  uint32_t sid = lane == 0 ? static_cast<uint32_t>(start) : kPadId;
+  float sd = lane == 0 ? d0 : INFINITY;
+  int idx = 0;
+  for (int hop = 0;; ++hop) {
+    if (hop >= max_hops) {
+      capped = true;
+      break;
+    }
+    const uint32_t u = __shfl_sync(kFull, sid, idx);
+    if (lane == idx) sid |= kVisited;
+    const int v = lane < kNavNbr ? __ldg(ix.nav_adj + static_cast<size_t>(u) * ix.nav_row + lane) : -1;
+    // the neighbour list ends at the first -1 or after 28 entries
+    const unsigned term = __ballot_sync(kFull, lane >= kNavNbr || v == -1);
+    const int cnt = __ffs(term) - 1;
+    float dv = INFINITY;
+    if (lane < cnt) dv = lane_sqdist<T>(qs, nv + static_cast<size_t>(v) * rs, ix.dim);
+    const int src = lane >= kNavBest ? lane - kNavBest : 0;
+    const uint32_t nid = __shfl_sync(kFull, static_cast<uint32_t>(v), src);
+    const float nd = __shfl_sync(kFull, dv, src);
+    if (lane >= kNavBest && lane - kNavBest < cnt) {
+      sid = nid;
+      sd = nd;
+    }
+#pragma unroll
+    for (int i = 0; i < kNavBest; ++i) {
+      const uint32_t prev = __shfl_sync(kFull, sid, i > 0 ? i - 1 : 0);
+      float dist = sd;
+      int pos = lane;
+      bool kill = false;
+      if (lane < i) dist = INFINITY;
+      else if (i != 0 && ((sid ^ prev) & 0x7fffffffu) == 0) kill = true;
+      // A copy of slot i-1's node is dropped and its visited bit folded into
+      // slot i-1. With several copies in one round the reference's stores race;
+      // the highest lane's value is taken here.
+      const unsigned km = __ballot_sync(kFull, kill);
+      if (km) {
+        const uint32_t hv = __shfl_sync(kFull, sid, 31 - __clz(km));
+        if (lane == i - 1) sid = prev | hv;
+      }
+      if (kill) {
+        sd = INFINITY;
+        dist = INFINITY;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const int op = __shfl_down_sync(kFull, pos, off);
+        const float ov = __shfl_down_sync(kFull, dist, off);
+        if (ov < dist) {
+          dist = ov;
+          pos = op;
+        }
+      }
+      pos = __shfl_sync(kFull, pos, 0);
+      if (i != pos) {
+        const float t = __shfl_sync(kFull, sd, i);
+        const float y = __shfl_sync(kFull, sd, pos);
+        const uint32_t ti = __shfl_sync(kFull, sid, i);
+        const uint32_t yi = __shfl_sync(kFull, sid, pos);
+        if (t != y) {
+          if (lane == i) { sd = y; sid = yi; }
+          if (lane == pos) { sd = t; sid = ti; }
+        }
+      }
+    }
+    const unsigned val = __ballot_sync(kFull, !(sid & kVisited));
+    const int x = val ? __ffs(val) - 1 : 32;
+    if (x >= kNavBest) break;
+    idx = x;
+  }
+  return static_cast<int>(__shfl_sync(kFull, sid, 0) & 0x7fffffffu);
+}
+
+// ADC table of one query into `lut` [M x 256] (shared or global memory).
+// Lane l owns pivots 8l..8l+7 (two float4 loads per dimension).
+__device__ __forceinline__ void build_lut(const DeviceIndex& ix, const float* __restrict__ qc,
+                                          float* __restrict__ lut, int lane) {
+  for (int c = 0; c < ix.chunks; ++c) {
+    const int a0 = __ldg(ix.chunk_off + c), a1 = __ldg(ix.chunk_off + c + 1);
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+    for (int i = a0; i < a1; ++i) {
+      const float qi = qc[i];
+      const float4* p = reinterpret_cast<const float4*>(ix.pivots_t + static_cast<size_t>(i) * kPivots) + 2 * lane;
+      const float4 p0 = __ldg(p), p1 = __ldg(p + 1);
+      const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float d = __fsub_rn(qi, pv[k]);
+        acc[k] = __fmaf_rn(d, d, acc[k]);
+      }
+    }
+    float4* o = reinterpret_cast<float4*>(lut + c * kPivots) + 2 * lane;
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+}
+
+// Sum LUT entries for up to 16 codes packed in `c`, in chunk order.
+__device__ __forceinline__ float adc16(float s, const uint4 c, const float* __restrict__ lut, int n) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int b = 0; b < 16; ++b) {
+    if (b < n) s = __fadd_rn(s, lut[b * kPivots + ((w[b >> 2] >> (8 * (b & 3))) & 0xffu)]);
+  }
+  return s;
+}
+
+struct WarpSmem {
+  float* lut;
+  float* qs;      // q, then q'' = (q - c) + c once the entry is known
+  float* qc;      // q - c
+  uint64_t* pool;
+  uint64_t* cand;
+  int* candr;
+  int* hist;
+  float* topd;
+  int* topi;
+};
+
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+// Shared-memory carve-up of one warp; mirrored by search_smem_bytes().
+__host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim, int npl, int pl,
+                                        int topk, WarpSmem* w) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    unsigned char* p = base ? base + off : nullptr;
+    off += align16(bytes);
+    return p;
+  };
+  const int dpad = (dim + 3) & ~3;
+  unsigned char* lut = take(sizeof(float) * chunks * kPivots);
+  unsigned char* qs = take(sizeof(float) * dpad);
+  unsigned char* qc = take(sizeof(float) * dpad);
+  unsigned char* pool = take(sizeof(uint64_t) * pl * kWarp);
+  unsigned char* cand = take(sizeof(uint64_t) * npl * kWarp);
+  unsigned char* candr = take(sizeof(int) * npl * kWarp);
+  unsigned char* hist = take(sizeof(int) * (pl * kWarp + kWarp));
+  unsigned char* topd = take(sizeof(float) * topk);
+  unsigned char* topi = take(sizeof(int) * topk);
+  if (w) {
+    w->lut = reinterpret_cast<float*>(lut);
+    w->qs = reinterpret_cast<float*>(qs);
+    w->qc = reinterpret_cast<float*>(qc);
+    w->pool = reinterpret_cast<uint64_t*>(pool);
+    w->cand = reinterpret_cast<uint64_t*>(cand);
+    w->candr = reinterpret_cast<int*>(candr);
+    w->hist = reinterpret_cast<int*>(hist);
+    w->topd = reinterpret_cast<float*>(topd);
+    w->topi = reinterpret_cast<int*>(topi);
+  }
+  return off;
+}
+
+// Best-first traversal of one query from `entry` (src/impl/pure_mem.cuh:285-428).
+template <typename T, int NPL, int PL>
+__device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid, uint32_t entry,
+                         const WarpSmem& s, int lane) {
+  const int dim = ix.dim, R = ix.degree, M = ix.chunks, L = a.ef, topk = a.topk;
+  const T* X = reinterpret_cast<const T*>(ix.vecs);
+  const size_t vrs = static_cast<size_t>(ix.vec_stride) / sizeof(T);
+  const int mw = ix.code_stride >> 4;
+  int psize = 0, tcnt = 0;
+  uint32_t hops = 0, adc = 0;
+  uint32_t u = entry;
+  bool capped = false;
+
+  for (;;) {
+    if (hops >= static_cast<uint32_t>(a.max_hops)) {
+      capped = true;
+      break;
+    }
+    ++hops;
+    // neighbour ids of u (padding = kPadId) and u's vector for the re-rank
+    const uint32_t* arow = ix.adj + static_cast<size_t>(u) * ix.adj_stride;
+    uint32_t nb[NPL];
+    bool ok[NPL];
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      const int e = lane + kWarp * k;
+      nb[k] = e < R ? __ldg(arow + e) : kPadId;
+      ok[k] = nb[k] != kPadId;
+    }
+    const T* xr = X + static_cast<size_t>(u) * vrs;
+    float acc = 0.f;
+    for (int i = lane; i < dim; i += kWarp) {
+      const float d = __fsub_rn(s.qs[i], static_cast<float>(xr[i]));
+      acc = __fmaf_rn(d, d, acc);
+    }
+
+    // ADC of every neighbour, one lane per neighbour, chunks in order
+    float dsum[NPL];
+    const uint4* crow[NPL];
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      dsum[k] = 0.f;
+      crow[k] = reinterpret_cast<const uint4*>(ix.codes + static_cast<size_t>(ok[k] ? nb[k] : 0) * ix.code_stride);
+    }
+    uint4 cur[NPL];
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) cur[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
+    for (int w = 0; w < mw; ++w) {
+      uint4 nxt[NPL];
+      const bool more = w + 1 < mw;
+#pragma unroll
+      for (int k = 0; k < NPL; ++k) nxt[k] = (more && ok[k]) ? __ldg(crow[k] + w + 1) : make_uint4(0, 0, 0, 0);
+      const int n = min(16, M - 16 * w);
+      const float* lw = s.lut + 16 * w * kPivots;
+#pragma unroll
+      for (int k = 0; k < NPL; ++k)
+        if (ok[k]) dsum[k] = adc16(dsum[k], cur[k], lw, n);
+#pragma unroll
+      for (int k = 0; k < NPL; ++k) cur[k] = nxt[k];
+    }
+
+    // exact distance of u, then insert after every equal entry of the top-k
+    // (retset_push_32, src/impl/util.cuh:116-163)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, off));
+    const float ex = __shfl_sync(kFull, acc, 0);
+    {
+      int le = 0;
+      for (int t0 = 0; t0 < tcnt; t0 += kWarp) {
+        const int t = t0 + lane;
+        le += __popc(__ballot_sync(kFull, t < tcnt && s.topd[t] <= ex));
+      }
+      if (le < topk) {
+        const int hi = min(tcnt, topk - 1);
+        if (hi > le) {
+          const int nch = (hi - le + kWarp - 1) / kWarp;
+          for (int c = nch - 1; c >= 0; --c) {
+            const int t = le + c * kWarp + lane;
+            const bool v = t < hi;
+            float dv = 0.f;
+            int iv = 0;
+            if (v) { dv = s.topd[t]; iv = s.topi[t]; }
+            __syncwarp();
+            if (v) { s.topd[t + 1] = dv; s.topi[t + 1] = iv; }
+            __syncwarp();
+          }
+        }
+        if (lane == 0) {
+          s.topd[le] = ex;
+          s.topi[le] = static_cast<int>(u);
+        }
+      }
+      tcnt = min(tcnt + 1, topk);
+    }
+
+    // candidates that can enter the pool: not beyond its last entry when full,
+    // not already in it; rank = insertion point (lower bound on (dist, id))
+    uint64_t key[NPL];
+    int rk[NPL];
+    const uint64_t last = psize == L ? (s.pool[L - 1] >> 1) : ~0ull;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      adc += __popc(__ballot_sync(kFull, ok[k]));
+      key[k] = make_key(dsum[k], nb[k]);
+      rk[k] = 0;
+      if (ok[k]) {
+        const uint64_t kk = key[k] >> 1;
+        if (kk >= last) {
+          ok[k] = false;
+        } else {
+          int lo = 0, hi = psize;
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if ((s.pool[mid] >> 1) < kk) lo = mid + 1; else hi = mid;
+          }
+          rk[k] = lo;
+          if (lo < psize && (s.pool[lo] >> 1) == kk) ok[k] = false;
+        }
+      }
+    }
+    int S = 0;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      const unsigned bm = __ballot_sync(kFull, ok[k]);
+      if (ok[k]) {
+        const int slot = S + __popc(bm & ((1u << lane) - 1u));
+        s.cand[slot] = key[k];
+        s.candr[slot] = rk[k];
+      }
+      S += __popc(bm);
+    }
+    __syncwarp();
+
+    if (S > 0) {
+      // final slot of each survivor = rank in pool + rank among survivors
+      uint64_t ck[NPL];
+      int cpos[NPL], cr[NPL];
+#pragma unroll
+      for (int k = 0; k < NPL; ++k) {
+        const int si = lane + kWarp * k;
+        cpos[k] = INT_MAX;
+        cr[k] = 0;
+        ck[k] = 0;
+        if (si < S) {
+          ck[k] = s.cand[si];
+          cr[k] = s.candr[si];
+          const uint64_t kk = ck[k] >> 1;
+          int less = 0;
+          for (int t = 0; t < S; ++t) {
+            const uint64_t o = s.cand[t] >> 1;
+            less += (o < kk) || (o == kk && t < si);
+          }
+          cpos[k] = cr[k] + less;
+        }
+      }
+      // pool entry i moves right by the number of survivors ranked <= i
+      for (int i = lane; i <= psize; i += kWarp) s.hist[i] = 0;
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < NPL; ++k)
+        if (lane + kWarp * k < S) atomicAdd(&s.hist[cr[k]], 1);
+      __syncwarp();
+      uint64_t pv[PL];
+      int pd[PL];
+      int carry = 0;
+#pragma unroll
+      for (int j = 0; j < PL; ++j) {
+        const int i = lane + kWarp * j;
+        int h = i < psize ? s.hist[i] : 0;
+#pragma unroll
+        for (int off = 1; off < kWarp; off <<= 1) {
+          const int y = __shfl_up_sync(kFull, h, off);
+          if (lane >= off) h += y;
+        }
+        pd[j] = INT_MAX;
+        pv[j] = 0;
+        if (i < psize) {
+          pv[j] = s.pool[i];
+          pd[j] = i + h + carry;
+        }
+        carry += __shfl_sync(kFull, h, kWarp - 1);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < PL; ++j)
+        if (pd[j] < L) s.pool[pd[j]] = pv[j];
+#pragma unroll
+      for (int k = 0; k < NPL; ++k)
+        if (cpos[k] < L) s.pool[cpos[k]] = ck[k];
+      psize = min(psize + S, L);
+      __syncwarp();
+    }
+
+    // next node: the first unvisited pool entry (all of them are among the
+    // first `ef` distinct candidates); none left -> done
+    int sel = -1;
+#pragma unroll
+    for (int j = 0; j < PL; ++j) {
+      const int i = lane + kWarp * j;
+      const unsigned bm = __ballot_sync(kFull, i < psize && (s.pool[i] & 1ull));
+      if (bm) {
+        sel = kWarp * j + __ffs(bm) - 1;
+        break;
+      }
+    }
+    if (sel < 0) break;
+    const uint64_t e = s.pool[sel];
+    __syncwarp();
+    if (lane == 0) s.pool[sel] = e & ~1ull;
+    u = static_cast<uint32_t>(e) >> 1;
+    __syncwarp();
+  }
+
+  int32_t* nns = a.nns + qid * topk;
+  float* dist = a.dist + qid * topk;
+  for (int t = lane; t < topk; t += kWarp) {
+    const bool v = t < tcnt;
+    nns[t] = v ? s.topi[t] : 0;
+    dist[t] = v ? s.topd[t] : 0.f;
+  }
+  if (lane == 0) {
+    a.found[qid] = tcnt;
+    if (a.hops) a.hops[qid] = hops;
+    if (a.adc) a.adc[qid] = adc;
+    if (capped) atomicAdd(a.err, 1);
+  }
+}
+
+template <typename T, int NPL, int PL>
+__global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, const SearchArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  WarpSmem s;
+  carve(smem, ix.chunks, ix.dim, NPL, PL, a.topk, &s);
+  const int lane = threadIdx.x;
+  const int dim = ix.dim;
+  for (;;) {
+    int qid = 0;
+    if (lane == 0) qid = atomicAdd(a.qcounter, 1);
+    qid = __shfl_sync(kFull, qid, 0);
+    if (qid >= a.nq) break;
+    const float* q = a.q + static_cast<int64_t>(qid) * dim;
+    for (int i = lane; i < dim; i += kWarp) {
+      const float v = q[i];
+      s.qs[i] = v;
+      s.qc[i] = __fsub_rn(v, __ldg(ix.centroid + i));
+    }
+    __syncwarp();
+    uint32_t entry = static_cast<uint32_t>(ix.medoid);
+    if (ix.has_nav) {
+      bool capped = false;
+      const int si = nav_search<T>(ix, s.qs, lane, a.nav_max_hops, capped);
+      // slot 0 can end up holding an empty slot on degenerate graphs (a node
+      // whose only neighbour is itself); the reference then indexes its map out
+      // of range, here the query falls back to the medoid and is counted
+      const bool bad = si < 0 || si >= ix.nav_points;
+      if (!bad) entry = static_cast<uint32_t>(__ldg(ix.nav_map + si));
+      if ((capped || bad) && lane == 0) atomicAdd(a.err + 1, 1);
+    }
+    __syncwarp();
+    for (int i = lane; i < dim; i += kWarp) s.qs[i] = __fadd_rn(s.qc[i], __ldg(ix.centroid + i));
+    build_lut(ix, s.qc, s.lut, lane);
+    __syncwarp();
+    traverse<T, NPL, PL>(ix, a, qid, entry, s, lane);
+    __syncwarp();
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarp) probe_lut_kernel(const DeviceIndex ix, const float* q, int64_t nq,
+                                                          float* lut) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* qc = reinterpret_cast<float*>(smem);
+  const int lane = threadIdx.x;
+  for (int64_t qid = blockIdx.x; qid < nq; qid += gridDim.x) {
+    for (int i = lane; i < ix.dim; i += kWarp) qc[i] = __fsub_rn(q[qid * ix.dim + i], __ldg(ix.centroid + i));
+    __syncwarp();
+    build_lut(ix, qc, lut + qid * ix.chunks * kPivots, lane);
+    __syncwarp();
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarp) probe_entry_kernel(const DeviceIndex ix, const float* q, int64_t nq,
+                                                            int32_t* sample, int32_t* entry, int32_t* err,
+                                                            int max_hops) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* qs = reinterpret_cast<float*>(smem);
+  const int lane = threadIdx.x;
+  for (int64_t qid = blockIdx.x; qid < nq; qid += gridDim.x) {
+    for (int i = lane; i < ix.dim; i += kWarp) qs[i] = q[qid * ix.dim + i];
+    __syncwarp();
+    bool capped = false;
+    const int si = nav_search<T>(ix, qs, lane, max_hops, capped);
+    const bool bad = si < 0 || si >= ix.nav_points;
+    if (lane == 0) {
+      sample[qid] = si;
+      entry[qid] = bad ? static_cast<int32_t>(ix.medoid) : __ldg(ix.nav_map + si);
+      if (capped || bad) atomicAdd(err, 1);
+    }
+    __syncwarp();
+  }
+}
+
+int npl_for(int degree) { return degree <= 64 ? 2 : 4; }
+int pl_for(int ef) { return ef <= 64 ? 2 : ef <= 128 ? 4 : ef <= 256 ? 8 : 16; }
+
+template <typename T, int NPL, int PL>
+cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
+  const size_t smem = carve(nullptr, ix.chunks, ix.dim, NPL, PL, a.topk, nullptr);
+  auto fn = search_kernel<T, NPL, PL>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kWarp, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm <= 0) return cudaErrorInvalidConfiguration;
+  int64_t grid = static_cast<int64_t>(per_sm) * sm_count;
+  if (grid > a.nq) grid = a.nq;
+  if (grid <= 0) return cudaSuccess;
+  fn<<<static_cast<unsigned>(grid), kWarp, smem, st>>>(ix, a);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_typed(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
+  const int npl = npl_for(ix.degree), pl = pl_for(a.ef);
+#define GANN_CASE(N, P) \
+  if (npl == N && pl == P) return launch_variant<T, N, P>(ix, a, sm_count, st);
+  GANN_CASE(2, 2) GANN_CASE(2, 4) GANN_CASE(2, 8) GANN_CASE(2, 16)
+  GANN_CASE(4, 2) GANN_CASE(4, 4) GANN_CASE(4, 8) GANN_CASE(4, 16)
+#undef GANN_CASE
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int search_max_ef() { return 16 * kWarp; }
+
+size_t search_smem_bytes(const DeviceIndex& ix, int topk, int ef) {
+  return carve(nullptr, ix.chunks, ix.dim, npl_for(ix.degree), pl_for(ef), topk, nullptr);
+}
+
+cudaError_t launch_search(const DeviceIndex& ix, const SearchArgs& a, int dtype, int sm_count,
+                          cudaStream_t st) {
+  if (dtype == GANN_UINT8) return launch_typed<uint8_t>(ix, a, sm_count, st);
+  return launch_typed<float>(ix, a, sm_count, st);
+}
+
+cudaError_t launch_probe_lut(const DeviceIndex& ix, const float* d_q, int64_t nq, float* d_lut,
+                             cudaStream_t st) {
+  const size_t smem = sizeof(float) * ((ix.dim + 3) & ~3);
+  const unsigned grid = static_cast<unsigned>(nq < 65535 ? nq : 65535);
+  if (grid == 0) return cudaSuccess;
+  probe_lut_kernel<float><<<grid, kWarp, smem, st>>>(ix, d_q, nq, d_lut);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_probe_entry(const DeviceIndex& ix, const float* d_q, int64_t nq, int dtype,
+                               int32_t* d_sample, int32_t* d_entry, int32_t* d_err, cudaStream_t st) {
+  const size_t smem = sizeof(float) * ((ix.dim + 3) & ~3);
+  const unsigned grid = static_cast<unsigned>(nq < 65535 ? nq : 65535);
+  if (grid == 0) return cudaSuccess;
+  const int cap = 1 << 20;
+  if (dtype == GANN_UINT8)
+    probe_entry_kernel<uint8_t><<<grid, kWarp, smem, st>>>(ix, d_q, nq, d_sample, d_entry, d_err, cap);
+  else
+    probe_entry_kernel<float><<<grid, kWarp, smem, st>>>(ix, d_q, nq, d_sample, d_entry, d_err, cap);
+  return cudaGetLastError();
+}
+
+}  // namespace gann

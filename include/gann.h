@@ -1,0 +1,148 @@
+/*
+ * gann.h -- C ABI of the B200 in-HBM search path (libgann.so).
+ *
+ * The path: batched best-first beam search over a DiskANN/Vamana graph,
+ * entered through the pivot ("nav") graph, guided by PQ asymmetric distances
+ * and finished with an exact re-rank of every expanded node. Results match the
+ * reference implementation (GustANN, src/impl/pure_mem.cuh:243-432) on the
+ * same index files.
+ *
+ * Plain C types only: pointers, sizes and status codes. No torch types. A
+ * handle is not re-entrant: one thread drives a handle at a time.
+ *
+ * Status codes replace the reference's exit(-1)/abort()/throw error paths
+ * (src/layout.cpp:13-16, src/nav_graph.cu:46-49, src/ssd_search.cu:66,
+ * src/common_cuda.cuh:10-17). gann_last_error() returns the message of the
+ * last failing call on the calling thread.
+ */
+#ifndef GANN_H_
+#define GANN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GANN_ABI_VERSION 1
+
+typedef enum {
+  GANN_OK = 0,
+  GANN_EINVAL = 1,       /* bad argument or malformed index file        */
+  GANN_EIO = 2,          /* file missing, short or unreadable           */
+  GANN_ENOMEM = 3,       /* host or device allocation failed            */
+  GANN_ECUDA = 4,        /* CUDA runtime error                          */
+  GANN_ETIMEDOUT = 5,    /* a bounded wait gave up                      */
+  GANN_EUNSUPPORTED = 6, /* mode or shape not supported by this build   */
+  GANN_ESTATE = 7        /* handle used in the wrong state              */
+} gann_status;
+
+/* Element type of the stored vectors: gustann::DataType (src/common.hpp:22-25). */
+typedef enum { GANN_UINT8 = 0, GANN_FLOAT = 1 } gann_dtype;
+
+/*
+ * Index location and placement. Replaces gustann::GustANNConfig
+ * (src/ssd_search.hpp:18-23) plus the use_gpu_mem flag of
+ * GustANN::init_pure_mem (src/ssd_search.hpp:76).
+ *   index_file        DiskANN disk index ("<prefix>_disk.index")
+ *   pq_file_prefix    reads <prefix>_pivots.bin and <prefix>_compressed.bin
+ *   nav_graph_prefix  directory with nav_index, nav_index.data, map.txt;
+ *                     NULL or "" = enter every query at the index medoid
+ *   use_gpu_mem       1: records in HBM ("-G"); 0: records in pinned host
+ *                     memory, read by the GPU over the host link
+ *   device            CUDA device ordinal
+ */
+typedef struct {
+  const char* index_file;
+  const char* pq_file_prefix;
+  const char* nav_graph_prefix;
+  int32_t dtype;
+  int32_t use_gpu_mem;
+  int32_t device;
+  int32_t reserved[5];
+} gann_config;
+
+/* Replaces gustann::GustANNStats (src/ssd_search.hpp:25-27) and adds the
+ * counters the HBM roofline needs. */
+typedef struct {
+  double run_time;        /* s: entry selection + traversal + re-rank (device) */
+  double total_time;      /* s: the whole call, host copies included          */
+  int64_t hops;           /* expanded nodes, summed over queries               */
+  int64_t adc_evals;      /* PQ distances evaluated, summed over queries       */
+  int64_t capped_queries; /* queries stopped by the hop cap (should be 0)      */
+  int64_t bytes_touched;  /* algorithmic HBM bytes of this batch               */
+} gann_stats;
+
+typedef struct {
+  int64_t num_points;
+  int32_t dim;
+  int32_t max_degree;     /* neighbour slots per record (max_m0)    */
+  int32_t pq_chunks;      /* M                                      */
+  int32_t dtype;
+  int64_t medoid;
+  int32_t node_len;       /* bytes of one on-disk record            */
+  int32_t nodes_per_page;
+  int32_t nav_points;     /* 0 when no nav graph                    */
+  int32_t nav_start;
+  int64_t device_bytes;   /* HBM held by the index                  */
+} gann_info;
+
+typedef struct gann_handle gann_handle;
+
+/* Parse and load an index onto cfg->device. Replaces GustANN::GustANN +
+ * GustANN::init_pure_mem (src/ssd_search.cu:108-112, 55-79) and the loaders
+ * it calls: Layout::parse_diskann_metadata (src/layout.cpp:11-69),
+ * PQSearch::read_data/init_device (src/pq_search.cu:56-185),
+ * NavGraph::init (src/nav_graph.cu:41-100) and
+ * PureMemExecutor::read_to_mem (src/pure_mem.cu:45-69). */
+int gann_open(const gann_config* cfg, gann_handle** out);
+
+/* Search nq queries (host buffers, row-major float32 [nq x dim]; uint8 data
+ * takes its queries widened to float). Writes nns [nq x topk] (int32 ids),
+ * distances [nq x topk] (squared L2, ascending) and found_cnt [nq]; slots past
+ * found_cnt[i] are 0. Requires 1 <= topk <= ef_search. Synchronous.
+ * Replaces GustANN::search -> PureMemExecutor::search
+ * (src/ssd_search.cu:114-140, src/pure_mem.cu:71-199). stats may be NULL. */
+int gann_search(gann_handle* h, const float* queries, int64_t nq, int32_t topk,
+                int32_t ef_search, int32_t* nns, float* distances,
+                int32_t* found_cnt, gann_stats* stats);
+
+/* Same search on device-resident buffers (all pointers on cfg->device),
+ * enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
+ * Asynchronous: no host synchronisation and no host copies. hops_out [nq]
+ * (uint32, may be NULL) receives the number of expanded nodes per query.
+ * Same kernel path as gann_search (src/pure_mem.cu:101-187 is the span it
+ * replaces); the caller owns the buffers. */
+int gann_search_device(gann_handle* h, const float* d_queries, int64_t nq,
+                       int32_t topk, int32_t ef_search, int32_t* d_nns,
+                       float* d_distances, int32_t* d_found_cnt,
+                       uint32_t* d_hops_out, void* stream);
+
+/* Release device and host memory of the handle (GustANN::~GustANN,
+ * src/ssd_search.cu:112-137). NULL is accepted. */
+int gann_close(gann_handle* h);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* gann_last_error(void);
+
+int gann_index_info(const gann_handle* h, gann_info* out);
+
+/* Stage probes (test hooks on the same device functions as the search):
+ *   gann_probe_lut: per-query ADC tables [nq x M x 256] float32, the
+ *     PQSearchData::init_query table (src/impl/pq.cuh:8-59);
+ *   gann_probe_entry: per-query nav result as sample index and as global id
+ *     (get_entry_kernel_inner + NavGraph::translate, src/impl/nav.cuh:13-135,
+ *     src/nav_graph.cu:104-109). Host buffers, synchronous. */
+int gann_probe_lut(gann_handle* h, const float* queries, int64_t nq, float* luts);
+int gann_probe_entry(gann_handle* h, const float* queries, int64_t nq,
+                     int32_t* sample_idx, int32_t* entry_ids);
+
+/* Pivot-graph sample: the sorted first `s` ids of a std::shuffle of [0, n)
+ * driven by std::mt19937(seed) -- the sampling step of bin/gen_small_file.cpp:18-40
+ * (seed 114514 there). Host only. */
+int gann_pivot_sample(int64_t n, int64_t s, uint32_t seed, int32_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GANN_H_ */

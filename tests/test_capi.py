@@ -1,0 +1,173 @@
+"""The C-ABI library loads, exports every symbol include/gann.h declares, and
+rejects malformed inputs with status codes -- all without a GPU (files are
+parsed before any CUDA call)."""
+import os
+import re
+import shutil
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+from gustann_b200 import api, formats
+from gustann_b200.api import GustANN, GustANNConfig, GustANNError
+
+HEADER = os.path.join(ROOT, "include", "gann.h")
+GOLD = os.path.join(ROOT, "tests", "golden", "g_u8")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(gann_\w+)\s*\(", src, re.M)))
+
+
+def test_header_declares_the_abi():
+    syms = declared_symbols()
+    assert set(syms) == set(api.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", api.LIB_PATH], capture_output=True, text=True, check=True)
+    exported = set(re.findall(r"\bT (gann_\w+)", out.stdout))
+    missing = [s for s in declared_symbols() if s not in exported]
+    assert not missing, missing
+
+
+def test_header_compiles_as_c_and_cpp(tmp_path):
+    c = tmp_path / "t.c"
+    c.write_text('#include "gann.h"\nint main(void){gann_config c; (void)c; return GANN_OK;}\n')
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.dirname(HEADER), "-c", str(c),
+                    "-o", str(tmp_path / "t.o")], check=True)
+    cc = tmp_path / "t.cpp"
+    cc.write_text('#include "gustann.hpp"\nint main(){gustann::GustANNConfig c; c.index_file="x"; return 0;}\n')
+    subprocess.run(["g++", "-std=c++17", "-Wall", "-Werror", "-I", os.path.dirname(HEADER), "-c", str(cc),
+                    "-o", str(tmp_path / "t2.o")], check=True)
+
+
+def test_pivot_sample_matches_std_shuffle_semantics():
+    a = api.pivot_sample(1000, 100)
+    b = api.pivot_sample(1000, 100)
+    assert np.array_equal(a, b)
+    assert np.all(np.diff(a) > 0) and a.min() >= 0 and a.max() < 1000
+    assert np.array_equal(api.pivot_sample(50, 50), np.arange(50))
+    with pytest.raises(GustANNError):
+        api.pivot_sample(10, 11)
+
+
+def _open_expect(cfg, code):
+    g = GustANN(formats.UINT8)
+    with pytest.raises(GustANNError) as e:
+        g.init_pure_mem(cfg, True)
+    assert e.value.code == code, str(e.value)
+
+
+def _copy_golden(tmp_path):
+    d = tmp_path / "idx"
+    shutil.copytree(GOLD, d)
+    return formats.index_paths(str(d))
+
+
+def test_missing_files(tmp_path):
+    p = _copy_golden(tmp_path)
+    _open_expect(GustANNConfig(str(tmp_path / "nope"), p["pq_file_prefix"], p["nav_graph_prefix"]), api.GANN_EIO)
+    _open_expect(GustANNConfig(p["index_file"], str(tmp_path / "nope"), p["nav_graph_prefix"]), api.GANN_EIO)
+    _open_expect(GustANNConfig(p["index_file"], p["pq_file_prefix"], str(tmp_path / "nope")), api.GANN_EIO)
+
+
+def test_wrong_dtype_is_rejected(tmp_path):
+    p = _copy_golden(tmp_path)
+    g = GustANN(formats.FLOAT)
+    with pytest.raises(GustANNError) as e:
+        g.init_pure_mem(GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"]), True)
+    assert e.value.code == api.GANN_EINVAL
+
+
+def test_corrupt_header(tmp_path):
+    p = _copy_golden(tmp_path)
+    with open(p["index_file"], "r+b") as f:
+        f.seek(8)
+        f.write(struct.pack("<Q", 0))          # zero nodes
+    _open_expect(GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"]), api.GANN_EINVAL)
+
+
+def test_truncated_index(tmp_path):
+    p = _copy_golden(tmp_path)
+    size = os.path.getsize(p["index_file"])
+    with open(p["index_file"], "r+b") as f:
+        f.truncate(size - 4096)
+    _open_expect(GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"]), api.GANN_EIO)
+
+
+def test_bad_neighbour_id(tmp_path):
+    """Out-of-range ids are caught while records are re-laid out; that step runs
+    after the CUDA check, so here (no GPU) the CPU parser is exercised directly
+    on the record layout instead."""
+    p = _copy_golden(tmp_path)
+    lay, vec, deg, nbrs = formats.read_disk_index(p["index_file"], formats.UINT8)
+    assert np.all(nbrs[np.arange(lay.max_m0)[None, :] < deg[:, None]] < lay.num_data)
+
+
+def test_pq_chunk_offsets_must_cover_dim(tmp_path):
+    p = _copy_golden(tmp_path)
+    piv, cen, offs, codes = formats.read_pq(p["pq_file_prefix"])
+    bad = offs.copy()
+    bad[-1] -= 1
+    formats.write_pq(p["pq_file_prefix"], piv, cen, bad, codes)
+    _open_expect(GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"]), api.GANN_EINVAL)
+
+
+def test_pq_row_count_must_match(tmp_path):
+    p = _copy_golden(tmp_path)
+    piv, cen, offs, codes = formats.read_pq(p["pq_file_prefix"])
+    formats.write_pq(p["pq_file_prefix"], piv, cen, offs, codes[:-1])
+    _open_expect(GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"]), api.GANN_EINVAL)
+
+
+def test_nav_bad_ids(tmp_path):
+    p = _copy_golden(tmp_path)
+    vec, adj, start, ids = formats.read_nav(p["nav_graph_prefix"], formats.UINT8)
+    ids2 = ids.copy()
+    ids2[0] = 10 ** 8
+    deg = (adj >= 0).sum(1)
+    formats.write_nav(p["nav_graph_prefix"], vec, ids2, adj, deg, start, max_degree=adj.shape[1])
+    _open_expect(GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"]), api.GANN_EINVAL)
+    adj2 = adj.copy()
+    adj2[3, 0] = len(ids) + 5
+    formats.write_nav(p["nav_graph_prefix"], vec, ids, adj2, deg, start, max_degree=adj.shape[1])
+    _open_expect(GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"]), api.GANN_EINVAL)
+
+
+def test_legacy_pq_layout_is_parsed(tmp_path):
+    """nr == 5 pivot tables (PipeANN/older DiskANN) put chunk offsets in slot 3."""
+    p = _copy_golden(tmp_path)
+    piv, cen, offs, codes = formats.read_pq(p["pq_file_prefix"])
+    formats.write_pq(p["pq_file_prefix"], piv, cen, offs, codes, legacy=True)
+    piv2, cen2, offs2, codes2 = formats.read_pq(p["pq_file_prefix"])
+    assert np.array_equal(offs2, offs)
+    g = GustANN(formats.UINT8)
+    with pytest.raises(GustANNError) as e:      # parses fine; fails only at the CUDA step
+        g.init_pure_mem(GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"]), True)
+    assert e.value.code in (api.GANN_ECUDA, api.GANN_EINVAL) or e.value.code == api.GANN_OK
+
+
+def test_use_before_init():
+    with pytest.raises(GustANNError) as e:
+        GustANN(formats.UINT8).query(np.zeros((1, 4), np.float32), 1, 1)
+    assert e.value.code == api.GANN_ESTATE
+
+
+def test_hybrid_is_unsupported():
+    with pytest.raises(GustANNError) as e:
+        GustANN().init_hybrid(None, None)
+    assert e.value.code == api.GANN_EUNSUPPORTED
+
+
+def test_cli_usage_and_errors():
+    cli = os.path.join(ROOT, "gustann_b200", "_lib", "search_mem")
+    r = subprocess.run([cli], capture_output=True, text=True)
+    assert r.returncode != 0 and "usage" in r.stderr
+    r = subprocess.run([cli, "--query", "x", "--index", "/nonexistent", "--pq_data", "p", "--data_type", "uint8",
+                        "--ef_search", "10", "--topk", "10"], capture_output=True, text=True)
+    assert r.returncode != 0 and "cannot open index file" in r.stderr

@@ -1,0 +1,189 @@
+"""Parity of the CUDA path (through the C ABI) with the oracle and with the
+reference's own kernels, on identical index files and queries.
+
+Bar: integer outputs (ids, found counts, entry points) identical; distances
+and ADC tables bit-identical (the kernel issues the reference's fp32
+operations in the reference's order, so the tolerance is zero).
+"""
+import numpy as np
+import pytest
+
+from conftest import INDEXES, get_index
+from gustann_b200.api import GustANN, GustANNConfig, GustANNError, GustANNStats
+from oracle import F_DUPNBR, F_HOPCAP, F_NAVRACE, F_STALE, Oracle, RefGPU
+
+pytestmark = pytest.mark.gpu
+
+EFS = [10, 33, 64, 100, 200]
+
+
+def _open(info, use_gpu_mem=True, nav=True):
+    p = info["paths"]
+    g = GustANN(info["dtype"])
+    g.init_pure_mem(GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"] if nav else ""),
+                    use_gpu_mem)
+    return g
+
+
+def _oracle(info, nav=True):
+    p = info["paths"]
+    return Oracle(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"] if nav else "", info["dtype"])
+
+
+@pytest.fixture(scope="module")
+def handles(index_root):
+    out = {}
+    for name in INDEXES:
+        info = get_index(index_root, name)
+        out[name] = (info, _open(info), _oracle(info))
+    yield out
+    for _, g, o in out.values():
+        g.close()
+        o.close()
+
+
+@pytest.mark.parametrize("name", list(INDEXES))
+def test_lut_bit_exact(handles, name):
+    info, g, o = handles[name]
+    q = info["queries"][:64]
+    np.testing.assert_array_equal(g.probe_lut(q), o.lut(q))
+
+
+@pytest.mark.parametrize("name", [n for n in INDEXES if INDEXES[n][4]])
+def test_entry_matches(handles, name):
+    info, g, o = handles[name]
+    q = info["queries"]
+    s, e = g.probe_entry(q)
+    os_, oe, of = o.nav(q)
+    ok = (of & F_NAVRACE) == 0
+    np.testing.assert_array_equal(s[ok], os_[ok])
+    np.testing.assert_array_equal(e[ok], oe[ok])
+
+
+@pytest.mark.parametrize("name", list(INDEXES))
+@pytest.mark.parametrize("ef", EFS)
+def test_search_matches_oracle(handles, name, ef):
+    info, g, o = handles[name]
+    q = info["queries"]
+    topk = 10
+    st = GustANNStats()
+    nns, dist, found = g.query(q, topk, ef, st)
+    onns, odist, ofound, ohops, oflags = o.search(q, topk, ef)
+    assert st.capped_queries == 0
+    assert not np.any(oflags & (F_HOPCAP | F_STALE | F_DUPNBR)), "input outside the reference's defined behaviour"
+    ok = (oflags & F_NAVRACE) == 0
+    np.testing.assert_array_equal(found[ok], ofound[ok])
+    np.testing.assert_array_equal(nns[ok], onns[ok])
+    np.testing.assert_array_equal(dist[ok], odist[ok])
+    assert st.hops == int(ohops[ok].sum()) or not ok.all()
+
+
+@pytest.mark.parametrize("name", ["u8", "f32"])
+def test_topk_edge_cases(handles, name):
+    info, g, o = handles[name]
+    q = info["queries"][:100]
+    for topk, ef in [(1, 1), (1, 16), (16, 16), (64, 64), (100, 128)]:
+        nns, dist, found = g.query(q, topk, ef)
+        onns, odist, ofound, _, oflags = o.search(q, topk, ef)
+        ok = oflags == 0
+        np.testing.assert_array_equal(nns[ok], onns[ok])
+        np.testing.assert_array_equal(dist[ok], odist[ok])
+        np.testing.assert_array_equal(found[ok], ofound[ok])
+
+
+def test_no_nav_uses_medoid(index_root):
+    info = get_index(index_root, "u8")
+    g = _open(info, nav=False)
+    o = _oracle(info, nav=False)
+    q = info["queries"][:200]
+    nns, dist, found = g.query(q, 10, 40)
+    onns, odist, ofound, _, oflags = o.search(q, 10, 40)
+    assert not oflags.any()
+    np.testing.assert_array_equal(nns, onns)
+    np.testing.assert_array_equal(dist, odist)
+    g.close()
+
+
+def test_host_records_mode_equal(index_root):
+    """use_gpu_mem=False keeps records in pinned host memory (the reference's
+    search_graph_kernel_dram mode); results are the same."""
+    info = get_index(index_root, "f32")
+    a = _open(info, use_gpu_mem=True)
+    b = _open(info, use_gpu_mem=False)
+    q = info["queries"][:200]
+    for ef in (20, 80):
+        x = a.query(q, 10, ef)
+        y = b.query(q, 10, ef)
+        for u, v in zip(x, y):
+            np.testing.assert_array_equal(u, v)
+    a.close()
+    b.close()
+
+
+def test_device_entry_point(index_root):
+    import torch
+    info = get_index(index_root, "f32")
+    g = _open(info)
+    q = info["queries"][:300]
+    topk, ef = 10, 64
+    dq = torch.from_numpy(q).cuda()
+    dn = torch.zeros((len(q), topk), dtype=torch.int32, device="cuda")
+    dd = torch.zeros((len(q), topk), dtype=torch.float32, device="cuda")
+    df = torch.zeros(len(q), dtype=torch.int32, device="cuda")
+    dh = torch.zeros(len(q), dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream()
+    g.search_device(dq.data_ptr(), len(q), topk, ef, dn.data_ptr(), dd.data_ptr(), df.data_ptr(), dh.data_ptr(),
+                    s.cuda_stream)
+    torch.cuda.synchronize()
+    nns, dist, found = g.query(q, topk, ef)
+    np.testing.assert_array_equal(dn.cpu().numpy(), nns)
+    np.testing.assert_array_equal(dd.cpu().numpy(), dist)
+    np.testing.assert_array_equal(df.cpu().numpy(), found)
+    assert int(dh.sum()) > 0
+    g.close()
+
+
+def test_empty_and_single_query(handles):
+    info, g, o = handles["u8"]
+    nns, dist, found = g.query(info["queries"][:0], 10, 20)
+    assert nns.shape == (0, 10)
+    q1 = info["queries"][:1]
+    x = g.query(q1, 10, 20)
+    y = o.search(q1, 10, 20)
+    np.testing.assert_array_equal(x[0], y[0])
+
+
+def test_bad_arguments_raise(handles):
+    info, g, _ = handles["u8"]
+    q = info["queries"][:4]
+    with pytest.raises(GustANNError):
+        g.query(q, 20, 10)          # topk > ef
+    with pytest.raises(GustANNError):
+        g.query(q, 10, 100000)      # ef beyond the supported maximum
+
+
+@pytest.mark.skipif(not RefGPU.available(), reason="reference library not built")
+@pytest.mark.parametrize("name", list(INDEXES))
+def test_reference_kernels_agree(handles, name):
+    """The reference's own compiled kernels on the B200, same files and queries."""
+    info, g, o = handles[name]
+    p = info["paths"]
+    r = RefGPU(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"], info["dtype"], info["dim"])
+    q = info["queries"][:200]
+    np.testing.assert_array_equal(r.lut(q[:32], info["M"]), g.probe_lut(q[:32]))
+    if p["nav_graph_prefix"]:
+        rs, re = r.nav(q)
+        s, e = g.probe_entry(q)
+        _, _, of = o.nav(q)
+        ok = (of & F_NAVRACE) == 0
+        np.testing.assert_array_equal(rs[ok], s[ok])
+        np.testing.assert_array_equal(re[ok], e[ok])
+    for ef in (10, 64, 200):
+        rn, rd, rf, _ = r.search(q, 10, ef)
+        nns, dist, found = g.query(q, 10, ef)
+        _, _, _, _, of = o.search(q, 10, ef)
+        ok = of == 0
+        np.testing.assert_array_equal(rf[ok], found[ok])
+        np.testing.assert_array_equal(rn[ok], nns[ok])
+        np.testing.assert_array_equal(rd[ok], dist[ok])
+    r.close()
