@@ -70,7 +70,9 @@ def test_search_matches_oracle(handles, name, ef):
     nns, dist, found = g.query(q, topk, ef, st)
     onns, odist, ofound, ohops, oflags = o.search(q, topk, ef)
     assert st.capped_queries == 0
-    assert not np.any(oflags & (F_HOPCAP | F_STALE | F_DUPNBR)), "input outside the reference's defined behaviour"
+    assert not np.any(oflags & (F_HOPCAP | F_DUPNBR)), "input outside the reference's defined behaviour"
+    # F_STALE queries (the reference would expand a slot it never wrote) stop in
+    # both the oracle and the kernel, so they are compared too
     ok = (oflags & F_NAVRACE) == 0
     np.testing.assert_array_equal(found[ok], ofound[ok])
     np.testing.assert_array_equal(nns[ok], onns[ok])
@@ -85,7 +87,7 @@ def test_topk_edge_cases(handles, name):
     for topk, ef in [(1, 1), (1, 16), (16, 16), (64, 64), (100, 128)]:
         nns, dist, found = g.query(q, topk, ef)
         onns, odist, ofound, _, oflags = o.search(q, topk, ef)
-        ok = oflags == 0
+        ok = (oflags & F_NAVRACE) == 0
         np.testing.assert_array_equal(nns[ok], onns[ok])
         np.testing.assert_array_equal(dist[ok], odist[ok])
         np.testing.assert_array_equal(found[ok], ofound[ok])
@@ -98,7 +100,7 @@ def test_no_nav_uses_medoid(index_root):
     q = info["queries"][:200]
     nns, dist, found = g.query(q, 10, 40)
     onns, odist, ofound, _, oflags = o.search(q, 10, 40)
-    assert not oflags.any()
+    assert not (oflags & (F_HOPCAP | F_DUPNBR)).any()
     np.testing.assert_array_equal(nns, onns)
     np.testing.assert_array_equal(dist, odist)
     g.close()
