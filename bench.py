@@ -57,10 +57,9 @@ def parse():
 
 
 def spec_for(args) -> datagen.MixtureSpec:
+    import dataclasses
     s = datagen.CONFIGS[args.config]
-    spec = datagen.MixtureSpec(s.kind, args.n or s.n, s.dim, s.centers, s.sigma, s.center_scale, s.zipf,
-                               s.query_noise)
-    return spec
+    return dataclasses.replace(s, n=args.n or s.n)
 
 
 # ------------------------------------------------------------------ plumbing

@@ -25,7 +25,7 @@ GANN_OK, GANN_EINVAL, GANN_EIO, GANN_ENOMEM, GANN_ECUDA, GANN_ETIMEDOUT, GANN_EU
 STATUS_NAMES = ["OK", "EINVAL", "EIO", "ENOMEM", "ECUDA", "ETIMEDOUT", "EUNSUPPORTED", "ESTATE"]
 
 # Every symbol include/gann.h declares.
-EXPORTS = ["gann_open", "gann_search", "gann_search_device", "gann_close", "gann_last_error",
+EXPORTS = ["gann_open", "gann_open_device", "gann_search", "gann_search_device", "gann_close", "gann_last_error",
            "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample"]
 
 
@@ -47,6 +47,15 @@ class _Stats(C.Structure):
                 ("adc_evals", C.c_int64), ("capped_queries", C.c_int64), ("bytes_touched", C.c_int64)]
 
 
+class _DeviceIndex(C.Structure):
+    _fields_ = [("vectors", C.c_void_p), ("vec_stride", C.c_int64), ("adjacency", C.c_void_p),
+                ("adj_stride", C.c_int32), ("max_degree", C.c_int32), ("codes", C.c_void_p),
+                ("code_stride", C.c_int32), ("pq_chunks", C.c_int32), ("pivots", C.c_void_p),
+                ("centroid", C.c_void_p), ("chunk_offsets", C.c_void_p), ("num_points", C.c_int64),
+                ("dim", C.c_int32), ("dtype", C.c_int32), ("medoid", C.c_int64), ("device", C.c_int32),
+                ("reserved", C.c_int32 * 3)]
+
+
 class _Info(C.Structure):
     _fields_ = [("num_points", C.c_int64), ("dim", C.c_int32), ("max_degree", C.c_int32),
                 ("pq_chunks", C.c_int32), ("dtype", C.c_int32), ("medoid", C.c_int64),
@@ -60,6 +69,7 @@ def _load() -> C.CDLL:
     lib = C.CDLL(LIB_PATH)
     vp, i64, i32, fp, ip = C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p
     lib.gann_open.argtypes = [C.POINTER(_Config), C.POINTER(vp)]
+    lib.gann_open_device.argtypes = [C.POINTER(_DeviceIndex), C.POINTER(vp)]
     lib.gann_search.argtypes = [vp, fp, i64, i32, i32, ip, fp, ip, C.POINTER(_Stats)]
     lib.gann_search_device.argtypes = [vp, vp, i64, i32, i32, vp, vp, vp, vp, vp]
     lib.gann_close.argtypes = [vp]
@@ -129,6 +139,28 @@ class GustANN:
         _check(lib.gann_open(C.byref(cfg), C.byref(h)))
         self._h = h
         self.dim = self.info()["dim"]
+
+    @classmethod
+    def from_device(cls, vectors, adjacency, codes, pivots: np.ndarray, centroid: np.ndarray,
+                    chunk_offsets: np.ndarray, medoid: int, max_degree: int, device: int = 0) -> "GustANN":
+        """Search over caller-owned CUDA tensors (``gann_open_device``): ``vectors``
+        [n, d] uint8/float32, ``adjacency`` [n, stride] int32 (-1 = empty slot),
+        ``codes`` [n, code_stride] uint8. The tensors must stay alive and may be
+        rewritten between searches."""
+        dt = UINT8 if vectors.dtype.itemsize == 1 else FLOAT
+        g = cls(dt, device)
+        piv = np.ascontiguousarray(pivots, np.float32)
+        cen = np.ascontiguousarray(centroid, np.float32)
+        off = np.ascontiguousarray(chunk_offsets, np.uint32)
+        d = _DeviceIndex(vectors.data_ptr(), vectors.stride(0) * vectors.element_size(), adjacency.data_ptr(),
+                         adjacency.stride(0), max_degree, codes.data_ptr(), codes.stride(0), len(off) - 1,
+                         _ptr(piv), _ptr(cen), _ptr(off), vectors.shape[0], vectors.shape[1], dt, medoid, device)
+        h = C.c_void_p()
+        _check(lib.gann_open_device(C.byref(d), C.byref(h)))
+        g._h = h
+        g.dim = int(vectors.shape[1])
+        g._keep = (vectors, adjacency, codes)
+        return g
 
     def init_hybrid(self, *args, **kwargs) -> None:
         """The SSD-tiered executor is not part of this build."""

@@ -48,6 +48,7 @@ struct gann_handle {
   int dtype = GANN_FLOAT;
   bool host_records = false;
   bool cuda_ready = false;           // a CUDA context exists for `device`
+  bool owns_records = true;          // false: vectors/adjacency/codes belong to the caller
   HostIndex hi;
   DeviceIndex ix;
   int sm_count = 0;
@@ -79,7 +80,11 @@ struct gann_handle {
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(device);
-    if (host_records) {
+    if (!owns_records) {
+      vecs = nullptr;
+      adj = nullptr;
+      codes = nullptr;
+    } else if (host_records) {
       if (vecs) cudaFreeHost(vecs);
       if (adj) cudaFreeHost(adj);
     } else {
@@ -220,6 +225,7 @@ int check_search_args(gann_handle* h, int64_t nq, int32_t topk, int32_t ef) {
   if (nq < 0 || nq >= (int64_t(1) << 31) - (int64_t(1) << 24))
     return set_error(GANN_EINVAL, "search: query count out of range");
   if (topk < 1 || topk > ef) return set_error(GANN_EINVAL, "search: need 1 <= topk <= ef_search");
+  if (h->hi.dim > 1024) return set_error(GANN_EUNSUPPORTED, "search: dimension above 1024");
   if (ef > gann::search_max_ef())
     return set_error(GANN_EUNSUPPORTED, "search: ef_search above " + std::to_string(gann::search_max_ef()));
   int per_sm_smem = 0;
@@ -257,9 +263,99 @@ int grow(T*& p, int64_t count) {
   return GANN_OK;
 }
 
+int open_device_impl(const gann_device_index* d, gann_handle* h) {
+  if (!d || !d->vectors || !d->adjacency || !d->codes || !d->pivots || !d->centroid || !d->chunk_offsets)
+    return set_error(GANN_EINVAL, "gann_open_device: null array");
+  if (d->dtype != GANN_UINT8 && d->dtype != GANN_FLOAT) return set_error(GANN_EINVAL, "gann_open_device: bad dtype");
+  const int elem = d->dtype == GANN_UINT8 ? 1 : 4;
+  if (d->num_points <= 0 || d->num_points >= (int64_t(1) << 31) || d->dim <= 0 || d->dim > 1024)
+    return set_error(GANN_EINVAL, "gann_open_device: bad size");
+  if (d->max_degree < 1 || d->max_degree > 128 || d->adj_stride < d->max_degree)
+    return set_error(GANN_EINVAL, "gann_open_device: bad degree / adjacency stride");
+  if (d->vec_stride < d->dim * elem || d->vec_stride % 16 || d->code_stride % 16 || d->pq_chunks < 1 ||
+      d->pq_chunks > 128 || d->code_stride < d->pq_chunks || d->adj_stride % 4)
+    return set_error(GANN_EINVAL, "gann_open_device: bad row strides");
+  if (d->medoid < 0 || d->medoid >= d->num_points) return set_error(GANN_EINVAL, "gann_open_device: bad medoid");
+  const uint32_t* off = d->chunk_offsets;
+  if (off[0] != 0 || off[d->pq_chunks] != static_cast<uint32_t>(d->dim))
+    return set_error(GANN_EINVAL, "gann_open_device: chunk offsets must span [0, dim]");
+  for (int i = 0; i < d->pq_chunks; ++i)
+    if (off[i + 1] <= off[i]) return set_error(GANN_EINVAL, "gann_open_device: chunk offsets must increase");
+  h->owns_records = false;
+  h->device = d->device;
+  h->dtype = d->dtype;
+  HostIndex& hi = h->hi;
+  hi.dtype = d->dtype;
+  hi.elem = elem;
+  hi.num_points = d->num_points;
+  hi.dim = d->dim;
+  hi.medoid = d->medoid;
+  hi.max_m0 = d->max_degree;
+  hi.data_size = d->dim * elem;
+  hi.max_node_len = hi.data_size + 4 * (d->max_degree + 1);
+  hi.num_chunks = d->pq_chunks;
+  hi.centroid.assign(d->centroid, d->centroid + d->dim);
+  hi.chunk_offsets.assign(off, off + d->pq_chunks + 1);
+  hi.pivots_t.resize(static_cast<size_t>(d->dim) * gann::kPivots);
+  for (int i = 0; i < gann::kPivots; ++i)
+    for (int j = 0; j < d->dim; ++j)
+      hi.pivots_t[static_cast<size_t>(j) * gann::kPivots + i] = d->pivots[static_cast<size_t>(i) * d->dim + j];
+  int ndev = 0;
+  GANN_CUDA(cudaGetDeviceCount(&ndev));
+  if (d->device < 0 || d->device >= ndev) return set_error(GANN_EINVAL, "gann_open_device: no such CUDA device");
+  GANN_CUDA(cudaSetDevice(h->device));
+  h->cuda_ready = true;
+  GANN_CUDA(cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, h->device));
+  GANN_CUDA(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+  GANN_CUDA(cudaEventCreate(&h->ev0));
+  GANN_CUDA(cudaEventCreate(&h->ev1));
+  int rc;
+  if ((rc = dev_upload(h->pivots_t, hi.pivots_t.data(), hi.pivots_t.size(), h->device_bytes))) return rc;
+  if ((rc = dev_upload(h->centroid, hi.centroid.data(), hi.centroid.size(), h->device_bytes))) return rc;
+  if ((rc = dev_upload(h->chunk_off, hi.chunk_offsets.data(), hi.chunk_offsets.size(), h->device_bytes))) return rc;
+  GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->counter), 4 * sizeof(int32_t)));
+  DeviceIndex& ix = h->ix;
+  ix.vecs = static_cast<const uint8_t*>(d->vectors);
+  ix.adj = d->adjacency;
+  ix.codes = d->codes;
+  ix.pivots_t = h->pivots_t;
+  ix.centroid = h->centroid;
+  ix.chunk_off = h->chunk_off;
+  ix.n = d->num_points;
+  ix.dim = d->dim;
+  ix.degree = d->max_degree;
+  ix.chunks = d->pq_chunks;
+  ix.vec_stride = d->vec_stride;
+  ix.adj_stride = d->adj_stride;
+  ix.code_stride = d->code_stride;
+  ix.medoid = d->medoid;
+  ix.has_nav = 0;
+  return GANN_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int gann_open_device(const gann_device_index* desc, gann_handle** out) {
+  if (!out) return set_error(GANN_EINVAL, "gann_open_device: out is NULL");
+  *out = nullptr;
+  gann_handle* h = new (std::nothrow) gann_handle();
+  if (!h) return set_error(GANN_ENOMEM, "gann_open_device: out of host memory");
+  int rc;
+  try {
+    rc = open_device_impl(desc, h);
+  } catch (const std::bad_alloc&) {
+    rc = set_error(GANN_ENOMEM, "gann_open_device: out of host memory");
+  }
+  if (rc != GANN_OK) {
+    h->release();
+    delete h;
+    return rc;
+  }
+  *out = h;
+  return GANN_OK;
+}
 
 int gann_open(const gann_config* cfg, gann_handle** out) {
   if (!out) return set_error(GANN_EINVAL, "gann_open: out is NULL");

@@ -274,18 +274,51 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
   return off;
 }
 
+// Neighbour ids (padding = kPadId) and the vector elements lane l owns
+// (dims l, l+32, ...) of one record.
+template <typename T, int NPL, int VP>
+__device__ __forceinline__ void load_node(const DeviceIndex& ix, uint32_t u, int lane, uint32_t (&nb)[NPL],
+                                          float (&xv)[VP]) {
+  const uint32_t* arow = ix.adj + static_cast<size_t>(u) * ix.adj_stride;
+#pragma unroll
+  for (int k = 0; k < NPL; ++k) {
+    const int e = lane + kWarp * k;
+    nb[k] = e < ix.degree ? __ldg(arow + e) : kPadId;
+  }
+  const T* xr = reinterpret_cast<const T*>(ix.vecs) + static_cast<size_t>(u) * (ix.vec_stride / sizeof(T));
+#pragma unroll
+  for (int v = 0; v < VP; ++v) {
+    const int i = lane + kWarp * v;
+    xv[v] = i < ix.dim ? static_cast<float>(__ldg(xr + i)) : 0.f;
+  }
+}
+
 // Best-first traversal of one query from `entry` (src/impl/pure_mem.cuh:285-428).
-template <typename T, int NPL, int PL>
+//
+// The node expanded next is min(first unvisited pool entry, best candidate
+// that enters the pool) -- exactly the first unvisited entry of the merged
+// pool -- so it is known right after the ADC step. Its record is requested
+// then, and the merge and the top-k insert of the current node run while that
+// load is in flight.
+template <typename T, int NPL, int PL, int VP>
 __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid, uint32_t entry,
                          const WarpSmem& s, int lane) {
-  const int dim = ix.dim, R = ix.degree, M = ix.chunks, L = a.ef, topk = a.topk;
-  const T* X = reinterpret_cast<const T*>(ix.vecs);
-  const size_t vrs = static_cast<size_t>(ix.vec_stride) / sizeof(T);
+  const int dim = ix.dim, M = ix.chunks, L = a.ef, topk = a.topk;
   const int mw = ix.code_stride >> 4;
   int psize = 0, tcnt = 0;
   uint32_t hops = 0, adc = 0;
   uint32_t u = entry;
   bool capped = false;
+
+  float qv[VP];   // q'' = (q - c) + c, the lane's dims
+#pragma unroll
+  for (int v = 0; v < VP; ++v) {
+    const int i = lane + kWarp * v;
+    qv[v] = i < dim ? s.qs[i] : 0.f;
+  }
+  uint32_t nb[NPL];
+  float xv[VP];
+  load_node<T, NPL, VP>(ix, u, lane, nb, xv);
 
   for (;;) {
     if (hops >= static_cast<uint32_t>(a.max_hops)) {
@@ -293,34 +326,33 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       break;
     }
     ++hops;
-    // neighbour ids of u (padding = kPadId) and u's vector for the re-rank
-    const uint32_t* arow = ix.adj + static_cast<size_t>(u) * ix.adj_stride;
-    uint32_t nb[NPL];
     bool ok[NPL];
+    const uint4* crow[NPL];
+    uint4 cur[NPL];
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
-      const int e = lane + kWarp * k;
-      nb[k] = e < R ? __ldg(arow + e) : kPadId;
       ok[k] = nb[k] != kPadId;
+      crow[k] = reinterpret_cast<const uint4*>(ix.codes + static_cast<size_t>(ok[k] ? nb[k] : 0) * ix.code_stride);
+      cur[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
     }
-    const T* xr = X + static_cast<size_t>(u) * vrs;
-    float acc = 0.f;
-    for (int i = lane; i < dim; i += kWarp) {
-      const float d = __fsub_rn(s.qs[i], static_cast<float>(xr[i]));
-      acc = __fmaf_rn(d, d, acc);
+
+    // first unvisited pool entry (the pool is as the last merge left it)
+    int ppos = -1;
+#pragma unroll
+    for (int j = 0; j < PL; ++j) {
+      const int i = lane + kWarp * j;
+      const unsigned bm = __ballot_sync(kFull, i < psize && (s.pool[i] & 1ull));
+      if (bm) {
+        ppos = kWarp * j + __ffs(bm) - 1;
+        break;
+      }
     }
+    const uint64_t pstar = ppos >= 0 ? s.pool[ppos] : ~0ull;
 
     // ADC of every neighbour, one lane per neighbour, chunks in order
     float dsum[NPL];
-    const uint4* crow[NPL];
 #pragma unroll
-    for (int k = 0; k < NPL; ++k) {
-      dsum[k] = 0.f;
-      crow[k] = reinterpret_cast<const uint4*>(ix.codes + static_cast<size_t>(ok[k] ? nb[k] : 0) * ix.code_stride);
-    }
-    uint4 cur[NPL];
-#pragma unroll
-    for (int k = 0; k < NPL; ++k) cur[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
+    for (int k = 0; k < NPL; ++k) dsum[k] = 0.f;
     for (int w = 0; w < mw; ++w) {
       uint4 nxt[NPL];
       const bool more = w + 1 < mw;
@@ -335,8 +367,61 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       for (int k = 0; k < NPL; ++k) cur[k] = nxt[k];
     }
 
-    // exact distance of u, then insert after every equal entry of the top-k
-    // (retset_push_32, src/impl/util.cuh:116-163)
+    // candidates that can enter the pool: not beyond its last entry when full,
+    // not already in it; rank = insertion point (lower bound on (dist, id))
+    uint64_t key[NPL];
+    int rk[NPL];
+    const uint64_t last = psize == L ? (s.pool[L - 1] >> 1) : ~0ull;
+    uint64_t mk = ~0ull;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      adc += __popc(__ballot_sync(kFull, ok[k]));
+      key[k] = make_key(dsum[k], nb[k]);
+      rk[k] = 0;
+      if (ok[k]) {
+        const uint64_t kk = key[k] >> 1;
+        if (kk >= last) {
+          ok[k] = false;
+        } else {
+          int lo = 0, hi = psize;
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if ((s.pool[mid] >> 1) < kk) lo = mid + 1; else hi = mid;
+          }
+          rk[k] = lo;
+          if (lo < psize && (s.pool[lo] >> 1) == kk) ok[k] = false;
+        }
+      }
+      if (ok[k] && key[k] < mk) mk = key[k];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const uint64_t o = __shfl_xor_sync(kFull, mk, off);
+      mk = o < mk ? o : mk;
+    }
+    const uint64_t nxt = mk < pstar ? mk : pstar;
+    const bool more = nxt != ~0ull;
+    uint32_t nb2[NPL];
+    float xv2[VP];
+    if (more) {
+      load_node<T, NPL, VP>(ix, static_cast<uint32_t>(nxt) >> 1, lane, nb2, xv2);
+    } else {
+#pragma unroll
+      for (int k = 0; k < NPL; ++k) nb2[k] = kPadId;
+#pragma unroll
+      for (int v = 0; v < VP; ++v) xv2[v] = 0.f;
+    }
+
+    // exact distance of u (lane-strided fma, shfl_down tree), then insert after
+    // every equal entry of the top-k (retset_push_32, src/impl/util.cuh:116-163)
+    float acc = 0.f;
+#pragma unroll
+    for (int v = 0; v < VP; ++v) {
+      if (lane + kWarp * v < dim) {
+        const float d = __fsub_rn(qv[v], xv[v]);
+        acc = __fmaf_rn(d, d, acc);
+      }
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, off));
     const float ex = __shfl_sync(kFull, acc, 0);
@@ -369,31 +454,8 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       tcnt = min(tcnt + 1, topk);
     }
 
-    // candidates that can enter the pool: not beyond its last entry when full,
-    // not already in it; rank = insertion point (lower bound on (dist, id))
-    uint64_t key[NPL];
-    int rk[NPL];
-    const uint64_t last = psize == L ? (s.pool[L - 1] >> 1) : ~0ull;
-#pragma unroll
-    for (int k = 0; k < NPL; ++k) {
-      adc += __popc(__ballot_sync(kFull, ok[k]));
-      key[k] = make_key(dsum[k], nb[k]);
-      rk[k] = 0;
-      if (ok[k]) {
-        const uint64_t kk = key[k] >> 1;
-        if (kk >= last) {
-          ok[k] = false;
-        } else {
-          int lo = 0, hi = psize;
-          while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if ((s.pool[mid] >> 1) < kk) lo = mid + 1; else hi = mid;
-          }
-          rk[k] = lo;
-          if (lo < psize && (s.pool[lo] >> 1) == kk) ok[k] = false;
-        }
-      }
-    }
+    // merge the surviving candidates into the pool; the entry equal to `nxt`
+    // is written back marked visited
     int S = 0;
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
@@ -406,7 +468,6 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       S += __popc(bm);
     }
     __syncwarp();
-
     if (S > 0) {
       // final slot of each survivor = rank in pool + rank among survivors
       uint64_t ck[NPL];
@@ -427,6 +488,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
             less += (o < kk) || (o == kk && t < si);
           }
           cpos[k] = cr[k] + less;
+          if (ck[k] == nxt) ck[k] &= ~1ull;
         }
       }
       // pool entry i moves right by the number of survivors ranked <= i
@@ -452,6 +514,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
         pv[j] = 0;
         if (i < psize) {
           pv[j] = s.pool[i];
+          if (pv[j] == nxt) pv[j] &= ~1ull;
           pd[j] = i + h + carry;
         }
         carry += __shfl_sync(kFull, h, kWarp - 1);
@@ -464,27 +527,16 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       for (int k = 0; k < NPL; ++k)
         if (cpos[k] < L) s.pool[cpos[k]] = ck[k];
       psize = min(psize + S, L);
-      __syncwarp();
+    } else if (more && lane == 0) {
+      s.pool[ppos] = pstar & ~1ull;   // no survivor: the next node is pool entry ppos
     }
-
-    // next node: the first unvisited pool entry (all of them are among the
-    // first `ef` distinct candidates); none left -> done
-    int sel = -1;
+    __syncwarp();
+    if (!more) break;
+    u = static_cast<uint32_t>(nxt) >> 1;
 #pragma unroll
-    for (int j = 0; j < PL; ++j) {
-      const int i = lane + kWarp * j;
-      const unsigned bm = __ballot_sync(kFull, i < psize && (s.pool[i] & 1ull));
-      if (bm) {
-        sel = kWarp * j + __ffs(bm) - 1;
-        break;
-      }
-    }
-    if (sel < 0) break;
-    const uint64_t e = s.pool[sel];
-    __syncwarp();
-    if (lane == 0) s.pool[sel] = e & ~1ull;
-    u = static_cast<uint32_t>(e) >> 1;
-    __syncwarp();
+    for (int k = 0; k < NPL; ++k) nb[k] = nb2[k];
+#pragma unroll
+    for (int v = 0; v < VP; ++v) xv[v] = xv2[v];
   }
 
   int32_t* nns = a.nns + qid * topk;
@@ -502,7 +554,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
   }
 }
 
-template <typename T, int NPL, int PL>
+template <typename T, int NPL, int PL, int VP>
 __global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, const SearchArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   WarpSmem s;
@@ -536,7 +588,7 @@ __global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, con
     for (int i = lane; i < dim; i += kWarp) s.qs[i] = __fadd_rn(s.qc[i], __ldg(ix.centroid + i));
     build_lut(ix, s.qc, s.lut, lane);
     __syncwarp();
-    traverse<T, NPL, PL>(ix, a, qid, entry, s, lane);
+    traverse<T, NPL, PL, VP>(ix, a, qid, entry, s, lane);
     __syncwarp();
   }
 }
@@ -579,11 +631,12 @@ __global__ void __launch_bounds__(kWarp) probe_entry_kernel(const DeviceIndex ix
 
 int npl_for(int degree) { return degree <= 64 ? 2 : 4; }
 int pl_for(int ef) { return ef <= 64 ? 2 : ef <= 128 ? 4 : ef <= 256 ? 8 : 16; }
+int vp_for(int dim) { return dim <= 128 ? 4 : 32; }
 
-template <typename T, int NPL, int PL>
+template <typename T, int NPL, int PL, int VP>
 cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
   const size_t smem = carve(nullptr, ix.chunks, ix.dim, NPL, PL, a.topk, nullptr);
-  auto fn = search_kernel<T, NPL, PL>;
+  auto fn = search_kernel<T, NPL, PL, VP>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   int per_sm = 0;
@@ -597,15 +650,21 @@ cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_co
   return cudaGetLastError();
 }
 
-template <typename T>
-cudaError_t launch_typed(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
+template <typename T, int VP>
+cudaError_t launch_vp(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
   const int npl = npl_for(ix.degree), pl = pl_for(a.ef);
 #define GANN_CASE(N, P) \
-  if (npl == N && pl == P) return launch_variant<T, N, P>(ix, a, sm_count, st);
+  if (npl == N && pl == P) return launch_variant<T, N, P, VP>(ix, a, sm_count, st);
   GANN_CASE(2, 2) GANN_CASE(2, 4) GANN_CASE(2, 8) GANN_CASE(2, 16)
   GANN_CASE(4, 2) GANN_CASE(4, 4) GANN_CASE(4, 8) GANN_CASE(4, 16)
 #undef GANN_CASE
   return cudaErrorInvalidValue;
+}
+
+template <typename T>
+cudaError_t launch_typed(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
+  if (vp_for(ix.dim) == 4) return launch_vp<T, 4>(ix, a, sm_count, st);
+  return launch_vp<T, 32>(ix, a, sm_count, st);
 }
 
 }  // namespace

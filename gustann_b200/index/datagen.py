@@ -5,8 +5,10 @@ from a Gaussian mixture with the shapes of the benchmark configurations:
 
 * ``sift``: centers uniform in ``[0, 128]^D``, per-dimension sigma, rounded and
   clipped to ``[0, 255]`` (uint8 records, SIFT-like).
-* ``deep``: centers ``N(0, center_scale^2 I)``, per-dimension sigma, every vector
-  L2-normalised (float32 records, DEEP-like).
+* ``deep``: centers ``N(0, center_scale^2 I)`` -- or, with ``center_rank`` r, drawn
+  on a random r-dimensional subspace with the same per-dimension scale (real
+  embedding sets have low intrinsic dimension) -- per-dimension sigma, every
+  vector L2-normalised (float32 records, DEEP-like).
 * ``text``: as ``deep`` but queries pick their cluster with a Zipf(1.1) law and get
   ``N(0, 0.05^2)`` noise (inner-product configuration).
 
@@ -37,6 +39,7 @@ class MixtureSpec:
     center_scale: float = 1.0
     zipf: float | None = None     # queries only (text)
     query_noise: float | None = None
+    center_rank: int | None = None  # deep/text: centers span a subspace of this rank
     seeds: dict = field(default_factory=lambda: {
         "centers": SEED_CENTERS, "data": SEED_DATA, "queries": SEED_QUERIES})
 
@@ -65,6 +68,11 @@ def centers(spec: MixtureSpec, device="cpu") -> torch.Tensor:
     g = _gen(device, spec.seeds["centers"], 0)
     if spec.kind == "sift":
         return torch.rand(spec.centers, spec.dim, generator=g, device=device) * 128.0
+    if spec.center_rank:
+        r = spec.center_rank
+        z = torch.randn(spec.centers, r, generator=g, device=device)
+        a = torch.randn(r, spec.dim, generator=g, device=device)
+        return (z @ a) * (spec.center_scale / r ** 0.5)
     return torch.randn(spec.centers, spec.dim, generator=g, device=device) * spec.center_scale
 
 

@@ -134,13 +134,14 @@ def knn_ivf(X: torch.Tensor, k: int, gen: torch.Generator, nlist: int | None = N
 
 
 def robust_prune(X: torch.Tensor, p_ids: torch.Tensor, cand: torch.Tensor, cand_d: torch.Tensor,
-                 R: int, alpha: float, batch: int = 1 << 14) -> torch.Tensor:
+                 R: int, alpha: float, batch: int = 1 << 14, return_dist: bool = False):
     """RobustPrune for many points at once.
 
     ``cand`` [B,K] candidate ids sorted nearest-first (-1 = empty), ``cand_d`` their
-    squared distances to ``p``. Returns [B,R] kept ids (-1 padded), nearest-first.
+    squared distances to ``p``. Returns [B,R] kept ids (-1 padded), nearest-first
+    (and their distances when ``return_dist``).
     """
-    out = []
+    out, outd = [], []
     for s in range(0, cand.shape[0], batch):
         ci = cand[s: s + batch]
         cd = cand_d[s: s + batch]
@@ -169,6 +170,12 @@ def robust_prune(X: torch.Tensor, p_ids: torch.Tensor, cand: torch.Tensor, cand_
         m = keep & (pos < R)
         res[rows[m], pos[m]] = ci[m]
         out.append(res)
+        if return_dist:
+            rd = torch.full((b, R), float("inf"), device=X.device)
+            rd[rows[m], pos[m]] = cd[m]
+            outd.append(rd)
+    if return_dist:
+        return torch.cat(out), torch.cat(outd)
     return torch.cat(out)
 
 

@@ -118,6 +118,41 @@ int gann_search_device(gann_handle* h, const float* d_queries, int64_t nq,
                        float* d_distances, int32_t* d_found_cnt,
                        uint32_t* d_hops_out, void* stream);
 
+/*
+ * A device-resident index the caller owns (no files): the arrays stay where
+ * the caller put them and must outlive the handle; the caller may rewrite
+ * `adjacency` between searches (an index builder refining its graph does).
+ * Layouts (all rows 16-byte aligned):
+ *   vectors    [n x vec_stride bytes], `dim` elements of `dtype` per row
+ *   adjacency  [n x adj_stride] uint32 neighbour ids, unused slots 0xffffffff
+ *   codes      [n x code_stride] uint8 PQ codes, code_stride % 16 == 0
+ * pivots [256 x dim], centroid [dim] and chunk_offsets [pq_chunks + 1] are host
+ * arrays in the PQ-file layout; they are copied. Searches enter at `medoid`.
+ * No counterpart in the reference, whose indexes are always loaded from files
+ * (src/ssd_search.cu:55-79); it serves graph construction on the GPU.
+ */
+typedef struct {
+  const void* vectors;
+  int64_t vec_stride;
+  const uint32_t* adjacency;
+  int32_t adj_stride;
+  int32_t max_degree;
+  const uint8_t* codes;
+  int32_t code_stride;
+  int32_t pq_chunks;
+  const float* pivots;
+  const float* centroid;
+  const uint32_t* chunk_offsets;
+  int64_t num_points;
+  int32_t dim;
+  int32_t dtype;
+  int64_t medoid;
+  int32_t device;
+  int32_t reserved[3];
+} gann_device_index;
+
+int gann_open_device(const gann_device_index* desc, gann_handle** out);
+
 /* Release device and host memory of the handle (GustANN::~GustANN,
  * src/ssd_search.cu:112-137). NULL is accepted. */
 int gann_close(gann_handle* h);
