@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--n", type=int, default=0, help="override the number of base points")
     ap.add_argument("--nq", type=int, default=10000)
     ap.add_argument("--target", type=float, default=0.9)
-    ap.add_argument("--efs", default="16,20,24,32,40,48,64,80,96,128,160,200,256")
+    ap.add_argument("--efs", default="16,20,24,28,32,36,40,48,56,64,72,80,96,112,128,160,200,256")
     ap.add_argument("--cache", default=os.environ.get("GANN_BENCH_CACHE", "/tmp/gann_bench"))
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -172,7 +172,7 @@ def traffic_per_launch(cfg_key: str):
 
 # ------------------------------------------------------------------ data
 def ensure_index(spec, args, d: Dist) -> dict:
-    key = f"{args.config}_n{spec.n}_R64_M32_v1"
+    key = f"{args.config}_n{spec.n}_R64_M32_v2"
     root = os.path.join(args.cache, key)
     done = os.path.join(root, "DONE")
     paths = formats.index_paths(root)
@@ -333,11 +333,13 @@ def run_ours(args, d: Dist):
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     d.barrier()
     torch.cuda.synchronize(dev)
+    torch.cuda.cudart().cudaProfilerStart()      # a profiler started with --profile-from-start off sees only this
     for a, b in evs:
         a.record(stream)
         launch()
         b.record(stream)
     torch.cuda.synchronize(dev)
+    torch.cuda.cudart().cudaProfilerStop()
     d.barrier()
     ck = clocks.stop()
     step_ms = [a.elapsed_time(b) for a, b in evs]

@@ -49,12 +49,15 @@ class MixtureSpec:
 
 
 # The five configurations of the benchmark description (sizes as stated there).
+# deep/text centers are random directions of unit expected norm (per-dimension
+# scale 1/sqrt(D)); sigma is per dimension before normalisation.
 CONFIGS = {
     "c0": MixtureSpec("sift", 1_000_000, 128, 1000, 20.0),
-    "c1": MixtureSpec("deep", 10_000_000, 96, 2000, 0.1),
+    "c1": MixtureSpec("deep", 10_000_000, 96, 2000, 0.1, center_scale=96 ** -0.5),
     "c2": MixtureSpec("sift", 100_000_000, 128, 10_000, 20.0),
     "c3": MixtureSpec("sift", 1_000_000_000, 128, 100_000, 20.0),
-    "c4": MixtureSpec("text", 10_000_000, 768, 5000, 0.1, zipf=1.1, query_noise=0.05),
+    "c4": MixtureSpec("text", 10_000_000, 768, 5000, 0.1 * (96 / 768) ** 0.5, center_scale=768 ** -0.5,
+                      zipf=1.1, query_noise=0.05),
 }
 
 
