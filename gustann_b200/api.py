@@ -26,7 +26,9 @@ STATUS_NAMES = ["OK", "EINVAL", "EIO", "ENOMEM", "ECUDA", "ETIMEDOUT", "EUNSUPPO
 
 # Every symbol include/gann.h declares.
 EXPORTS = ["gann_open", "gann_open_device", "gann_search", "gann_search_device", "gann_close", "gann_last_error",
-           "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample"]
+           "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample", "gann_set_option"]
+GANN_OPT_ADC_MODE, GANN_OPT_PIVOT_WARPS = 1, 2
+ADC_AUTO, ADC_TABLE, ADC_PIVOT = 0, 1, 2
 
 
 class GustANNError(RuntimeError):
@@ -78,6 +80,7 @@ def _load() -> C.CDLL:
     lib.gann_probe_lut.argtypes = [vp, fp, i64, fp]
     lib.gann_probe_entry.argtypes = [vp, fp, i64, ip, ip]
     lib.gann_pivot_sample.argtypes = [i64, i64, C.c_uint32, ip]
+    lib.gann_set_option.argtypes = [vp, i32, i64]
     for name in EXPORTS:
         if name != "gann_last_error":
             getattr(lib, name).restype = C.c_int
@@ -223,6 +226,11 @@ class GustANN:
         e = np.zeros(q.shape[0], np.int32)
         _check(lib.gann_probe_entry(self._h, _ptr(q), q.shape[0], _ptr(s), _ptr(e)))
         return s, e
+
+    def set_option(self, option: int, value: int) -> None:
+        """``gann_set_option``: ADC mode (0 auto, 1 table, 2 pivot) or pivot warps."""
+        self._need()
+        _check(lib.gann_set_option(self._h, option, value))
 
     def info(self) -> dict:
         self._need()

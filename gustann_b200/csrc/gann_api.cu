@@ -61,6 +61,7 @@ struct gann_handle {
   float* pivots_t = nullptr;
   float* centroid = nullptr;
   int32_t* chunk_off = nullptr;
+  float* piv4 = nullptr;
   uint8_t* nav_vecs = nullptr;
   int32_t* nav_adj = nullptr;
   int32_t* nav_map = nullptr;
@@ -92,7 +93,7 @@ struct gann_handle {
       if (adj) cudaFree(adj);
     }
     for (void* p : {static_cast<void*>(codes), static_cast<void*>(pivots_t), static_cast<void*>(centroid),
-                    static_cast<void*>(chunk_off), static_cast<void*>(nav_vecs), static_cast<void*>(nav_adj),
+                    static_cast<void*>(chunk_off), static_cast<void*>(piv4), static_cast<void*>(nav_vecs), static_cast<void*>(nav_adj),
                     static_cast<void*>(nav_map), static_cast<void*>(counter), static_cast<void*>(d_q),
                     static_cast<void*>(d_nns), static_cast<void*>(d_dist), static_cast<void*>(d_found),
                     static_cast<void*>(d_hops), static_cast<void*>(d_adc)})
@@ -148,6 +149,18 @@ int load_records(gann_handle* h, const std::string& path) {
   return GANN_OK;
 }
 
+int upload_pivot_table(gann_handle* h) {
+  std::vector<float> tab;
+  const int w = gann::make_pivot_table(h->hi.pivots_t, h->hi.chunk_offsets, static_cast<int>(h->hi.dim), tab);
+  if (w > 0) {
+    int rc = dev_upload(h->piv4, tab.data(), tab.size(), h->device_bytes);
+    if (rc) return rc;
+    h->ix.piv4 = reinterpret_cast<const float4*>(h->piv4);
+  }
+  h->ix.piv_width = w;
+  return GANN_OK;
+}
+
 int open_impl(const gann_config* cfg, gann_handle* h) {
   if (!cfg || !cfg->index_file || !cfg->pq_file_prefix)
     return set_error(GANN_EINVAL, "gann_open: index_file and pq_file_prefix are required");
@@ -200,6 +213,7 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
   ix.pivots_t = h->pivots_t;
   ix.centroid = h->centroid;
   ix.chunk_off = h->chunk_off;
+  if ((rc = upload_pivot_table(h))) return rc;
   if (hi.has_nav) {
     if ((rc = dev_upload(h->nav_vecs, hi.nav_vecs.data(), hi.nav_vecs.size(), h->device_bytes))) return rc;
     if ((rc = dev_upload(h->nav_adj, hi.nav_adj.data(), hi.nav_adj.size(), h->device_bytes))) return rc;
@@ -330,7 +344,7 @@ int open_device_impl(const gann_device_index* d, gann_handle* h) {
   ix.code_stride = d->code_stride;
   ix.medoid = d->medoid;
   ix.has_nav = 0;
-  return GANN_OK;
+  return upload_pivot_table(h);
 }
 
 }  // namespace
@@ -385,6 +399,25 @@ int gann_close(gann_handle* h) {
 }
 
 const char* gann_last_error(void) { return g_last_error.c_str(); }
+
+int gann_set_option(gann_handle* h, int32_t option, int64_t value) {
+  if (!h) return set_error(GANN_EINVAL, "gann_set_option: null handle");
+  switch (option) {
+    case GANN_OPT_ADC_MODE:
+      if (value < 0 || value > 2) return set_error(GANN_EINVAL, "gann_set_option: ADC mode must be 0, 1 or 2");
+      if (value == 2 && (h->ix.piv_width == 0 || h->ix.dim > 128))
+        return set_error(GANN_EUNSUPPORTED, "gann_set_option: pivot mode needs <= 4 dims per chunk and dim <= 128");
+      h->ix.adc_mode = static_cast<int32_t>(value);
+      return GANN_OK;
+    case GANN_OPT_PIVOT_WARPS:
+      if (value != 0 && (value < 8 || value > 24))
+        return set_error(GANN_EINVAL, "gann_set_option: pivot warps must be 0 or 8..24");
+      h->ix.piv_warps = static_cast<int32_t>(value);
+      return GANN_OK;
+    default:
+      return set_error(GANN_EINVAL, "gann_set_option: unknown option");
+  }
+}
 
 int gann_index_info(const gann_handle* h, gann_info* out) {
   if (!h || !out) return set_error(GANN_EINVAL, "gann_index_info: null argument");

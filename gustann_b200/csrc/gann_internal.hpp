@@ -62,6 +62,12 @@ struct DeviceIndex {
   int32_t nav_start = 0, has_nav = 0, nav_row = 0;
   int64_t nav_points = 0;
   int64_t medoid = 0;
+  // pivot table [M x 256] float4, chunk dims zero-padded to 4; piv_width = 3
+  // when every chunk has 3 dims, 4 when all have <= 4, 0 when a chunk is wider
+  const float4* piv4 = nullptr;
+  int32_t piv_width = 0;
+  int32_t adc_mode = 0;     // 0 auto, 1 table, 2 pivot
+  int32_t piv_warps = 0;    // 0 = as many as fit (<= 24)
 };
 
 struct SearchArgs {
@@ -87,6 +93,10 @@ cudaError_t launch_probe_entry(const DeviceIndex& ix, const float* d_q, int64_t 
                                int dtype, int32_t* d_sample, int32_t* d_entry,
                                int32_t* d_err, cudaStream_t st);
 size_t search_smem_bytes(const DeviceIndex& ix, int topk, int ef);
+// Pivot table of the pivot-mode kernel from the [256 x dim] PQ pivots; returns
+// the width code (see DeviceIndex::piv_width) and fills `out` when it is > 0.
+int make_pivot_table(const std::vector<float>& pivots_t, const std::vector<int32_t>& chunk_off, int dim,
+                     std::vector<float>& out);
 int search_max_ef();
 
 // Loader (gann_loader.cpp). Return GANN_* and fill `msg` on error.

@@ -18,6 +18,7 @@
 // of merge(pool, neighbours) with the pool copy first on equal keys, which is
 // what the reference's merge + 2L cut + dedup produce
 // (src/impl/pure_mem.cuh:350-419).
+#include <algorithm>
 #include <cstdint>
 #include <climits>
 
@@ -227,8 +228,41 @@ __device__ __forceinline__ float adc16(float s, const uint4 c, const float* __re
   return s;
 }
 
+// The same sums without a per-query table: the table entry of chunk `b` and
+// code `j` is recomputed from the CTA-resident pivot row piv[b][j] (zero-padded
+// to 4 dims) and the query residual qcp[b] -- d = qc_i - p_ji, e = fma(d, d, e)
+// from 0 over the chunk's dims in order, then s += e -- which are the fp32
+// operations that produce and consume the reference's table entry, so the sum
+// is bit-identical. CW = dims per chunk (4 also serves mixed widths <= 4: the
+// zero padding contributes fma(0, 0, e) = e).
+template <int CW>
+__device__ __forceinline__ float adc16_piv(float s, const uint4 c, const float4* __restrict__ piv,
+                                           const float4* __restrict__ qcp, int n) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int b = 0; b < 16; ++b) {
+    if (b < n) {
+      const float4 q = qcp[b];
+      const float4 p = piv[b * kPivots + ((w[b >> 2] >> (8 * (b & 3))) & 0xffu)];
+      float d = __fsub_rn(q.x, p.x);
+      float e = __fmul_rn(d, d);
+      d = __fsub_rn(q.y, p.y);
+      e = __fmaf_rn(d, d, e);
+      d = __fsub_rn(q.z, p.z);
+      e = __fmaf_rn(d, d, e);
+      if (CW > 3) {
+        d = __fsub_rn(q.w, p.w);
+        e = __fmaf_rn(d, d, e);
+      }
+      s = __fadd_rn(s, e);
+    }
+  }
+  return s;
+}
+
 struct WarpSmem {
-  float* lut;
+  float* lut;     // per-query ADC table (table mode)
+  float4* qcp;    // per-chunk query residuals, 4 dims padded (pivot mode)
   float* qs;      // q, then q'' = (q - c) + c once the entry is known
   float* qc;      // q - c
   uint64_t* pool;
@@ -243,7 +277,7 @@ __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(
 
 // Shared-memory carve-up of one warp; mirrored by search_smem_bytes().
 __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim, int npl, int pl,
-                                        int topk, WarpSmem* w) {
+                                        int topk, WarpSmem* w, bool piv = false) {
   size_t off = 0;
   auto take = [&](size_t bytes) {
     unsigned char* p = base ? base + off : nullptr;
@@ -251,7 +285,8 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
     return p;
   };
   const int dpad = (dim + 3) & ~3;
-  unsigned char* lut = take(sizeof(float) * chunks * kPivots);
+  unsigned char* lut = piv ? nullptr : take(sizeof(float) * chunks * kPivots);
+  unsigned char* qcp = piv ? take(sizeof(float4) * chunks) : nullptr;
   unsigned char* qs = take(sizeof(float) * dpad);
   unsigned char* qc = take(sizeof(float) * dpad);
   unsigned char* pool = take(sizeof(uint64_t) * pl * kWarp);
@@ -262,6 +297,7 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
   unsigned char* topi = take(sizeof(int) * topk);
   if (w) {
     w->lut = reinterpret_cast<float*>(lut);
+    w->qcp = reinterpret_cast<float4*>(qcp);
     w->qs = reinterpret_cast<float*>(qs);
     w->qc = reinterpret_cast<float*>(qc);
     w->pool = reinterpret_cast<uint64_t*>(pool);
@@ -300,9 +336,9 @@ __device__ __forceinline__ void load_node(const DeviceIndex& ix, uint32_t u, int
 // pool -- so it is known right after the ADC step. Its record is requested
 // then, and the merge and the top-k insert of the current node run while that
 // load is in flight.
-template <typename T, int NPL, int PL, int VP>
+template <typename T, int NPL, int PL, int VP, int PIV>
 __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid, uint32_t entry,
-                         const WarpSmem& s, int lane) {
+                         const WarpSmem& s, const float4* __restrict__ piv, int lane) {
   const int dim = ix.dim, M = ix.chunks, L = a.ef, topk = a.topk;
   const int mw = ix.code_stride >> 4;
   int psize = 0, tcnt = 0;
@@ -359,10 +395,19 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
 #pragma unroll
       for (int k = 0; k < NPL; ++k) nxt[k] = (more && ok[k]) ? __ldg(crow[k] + w + 1) : make_uint4(0, 0, 0, 0);
       const int n = min(16, M - 16 * w);
-      const float* lw = s.lut + 16 * w * kPivots;
+      if (PIV == 0) {
+        const float* lw = s.lut + 16 * w * kPivots;
 #pragma unroll
-      for (int k = 0; k < NPL; ++k)
-        if (ok[k]) dsum[k] = adc16(dsum[k], cur[k], lw, n);
+        for (int k = 0; k < NPL; ++k)
+          if (ok[k]) dsum[k] = adc16(dsum[k], cur[k], lw, n);
+      } else {
+        const float4* pw = piv + 16 * w * kPivots;
+        const float4* qw = s.qcp + 16 * w;
+#pragma unroll
+        for (int k = 0; k < NPL; ++k)
+          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3>(dsum[k], cur[k], pw, qw, n)
+                                        : adc16_piv<4>(dsum[k], cur[k], pw, qw, n);
+      }
 #pragma unroll
       for (int k = 0; k < NPL; ++k) cur[k] = nxt[k];
     }
@@ -554,12 +599,10 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
   }
 }
 
-template <typename T, int NPL, int PL, int VP>
-__global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, const SearchArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  WarpSmem s;
-  carve(smem, ix.chunks, ix.dim, NPL, PL, a.topk, &s);
-  const int lane = threadIdx.x;
+// One query per warp, from query setup to the written top-k.
+template <typename T, int NPL, int PL, int VP, int PIV>
+__device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchArgs& a, const WarpSmem& s,
+                                            const float4* __restrict__ piv, int lane) {
   const int dim = ix.dim;
   for (;;) {
     int qid = 0;
@@ -586,11 +629,48 @@ __global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, con
     }
     __syncwarp();
     for (int i = lane; i < dim; i += kWarp) s.qs[i] = __fadd_rn(s.qc[i], __ldg(ix.centroid + i));
-    build_lut(ix, s.qc, s.lut, lane);
+    if (PIV == 0) {
+      build_lut(ix, s.qc, s.lut, lane);
+    } else {
+      for (int c = lane; c < ix.chunks; c += kWarp) {
+        const int a0 = __ldg(ix.chunk_off + c), a1 = __ldg(ix.chunk_off + c + 1);
+        float r[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r[i] = a0 + i < a1 ? s.qc[a0 + i] : 0.f;
+        s.qcp[c] = make_float4(r[0], r[1], r[2], r[3]);
+      }
+    }
     __syncwarp();
-    traverse<T, NPL, PL, VP>(ix, a, qid, entry, s, lane);
+    traverse<T, NPL, PL, VP, PIV>(ix, a, qid, entry, s, piv, lane);
     __syncwarp();
   }
+}
+
+// Table mode: one warp per CTA, the warp's ADC table in its shared memory.
+template <typename T, int NPL, int PL, int VP>
+__global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, const SearchArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  WarpSmem s;
+  carve(smem, ix.chunks, ix.dim, NPL, PL, a.topk, &s, false);
+  run_queries<T, NPL, PL, VP, 0>(ix, a, s, nullptr, threadIdx.x);
+}
+
+// Pivot mode: one persistent CTA per SM holds the 256 x D pivot table once
+// (M x 4 KB) and runs up to kPivWarps queries at a time, one per warp, each
+// with ~2-8 KB of private state instead of a 4*M KB table.
+constexpr int kPivWarps = 24;
+template <typename T, int NPL, int PL, int VP, int CW>
+__global__ void __launch_bounds__(kWarp * kPivWarps, 1) search_kernel_piv(const DeviceIndex ix, const SearchArgs a,
+                                                                          size_t per_warp) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float4* piv = reinterpret_cast<float4*>(smem);
+  const int ntab = ix.chunks * kPivots;
+  for (int i = threadIdx.x; i < ntab; i += blockDim.x) piv[i] = __ldg(ix.piv4 + i);
+  __syncthreads();
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  WarpSmem s;
+  carve(smem + sizeof(float4) * ntab + per_warp * warp, ix.chunks, ix.dim, NPL, PL, a.topk, &s, true);
+  run_queries<T, NPL, PL, VP, CW>(ix, a, s, piv, lane);
 }
 
 template <typename T>
@@ -635,7 +715,28 @@ int vp_for(int dim) { return dim <= 128 ? 4 : 32; }
 
 template <typename T, int NPL, int PL, int VP>
 cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
-  const size_t smem = carve(nullptr, ix.chunks, ix.dim, NPL, PL, a.topk, nullptr);
+  int dev = 0, optin = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if constexpr (VP == 4) if (ix.piv_width > 0 && ix.adc_mode != 1) {
+    // pivot mode when the table plus at least 8 warps' state fit (dims <= 128;
+    // wider vectors have too many chunks for a shared-memory pivot table)
+    const size_t tab = sizeof(float4) * ix.chunks * kPivots;
+    const size_t per_warp = carve(nullptr, ix.chunks, ix.dim, NPL, PL, a.topk, nullptr, true);
+    int warps = static_cast<int>(std::min<size_t>(kPivWarps, (optin - tab) / per_warp));
+    if (ix.piv_warps > 0) warps = std::min(warps, ix.piv_warps);
+    if (tab < static_cast<size_t>(optin) && warps >= 8) {
+      const size_t smem = tab + per_warp * warps;
+      auto fn = ix.piv_width == 3 ? search_kernel_piv<T, NPL, PL, VP, 3> : search_kernel_piv<T, NPL, PL, VP, 4>;
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      int64_t grid = std::min<int64_t>(sm_count, (a.nq + warps - 1) / warps);
+      if (grid <= 0) return cudaSuccess;
+      fn<<<static_cast<unsigned>(grid), kWarp * warps, smem, st>>>(ix, a, per_warp);
+      return cudaGetLastError();
+    }
+  }
+  const size_t smem = carve(nullptr, ix.chunks, ix.dim, NPL, PL, a.topk, nullptr, false);
   auto fn = search_kernel<T, NPL, PL, VP>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -670,6 +771,26 @@ cudaError_t launch_typed(const DeviceIndex& ix, const SearchArgs& a, int sm_coun
 }  // namespace
 
 int search_max_ef() { return 16 * kWarp; }
+
+int make_pivot_table(const std::vector<float>& pivots_t, const std::vector<int32_t>& chunk_off, int dim,
+                     std::vector<float>& out) {
+  const int m = static_cast<int>(chunk_off.size()) - 1;
+  int maxw = 0;
+  bool all3 = true;
+  for (int c = 0; c < m; ++c) {
+    const int w = chunk_off[c + 1] - chunk_off[c];
+    maxw = std::max(maxw, w);
+    all3 = all3 && w == 3;
+  }
+  if (m <= 0 || maxw > 4 || static_cast<int64_t>(pivots_t.size()) < static_cast<int64_t>(dim) * kPivots) return 0;
+  out.assign(static_cast<size_t>(m) * kPivots * 4, 0.f);
+  for (int c = 0; c < m; ++c)
+    for (int j = 0; j < kPivots; ++j)
+      for (int i = 0; i < chunk_off[c + 1] - chunk_off[c]; ++i)
+        out[(static_cast<size_t>(c) * kPivots + j) * 4 + i] =
+            pivots_t[static_cast<size_t>(chunk_off[c] + i) * kPivots + j];
+  return all3 ? 3 : 4;
+}
 
 size_t search_smem_bytes(const DeviceIndex& ix, int topk, int ef) {
   return carve(nullptr, ix.chunks, ix.dim, npl_for(ix.degree), pl_for(ef), topk, nullptr);

@@ -157,6 +157,15 @@ int gann_open_device(const gann_device_index* desc, gann_handle** out);
  * src/ssd_search.cu:112-137). NULL is accepted. */
 int gann_close(gann_handle* h);
 
+/* Tuning options (no counterpart in the reference).
+ *   GANN_OPT_ADC_MODE: 0 auto, 1 per-query ADC table in shared memory, 2 the
+ *     PQ pivot table resident once per SM with table entries recomputed per
+ *     lookup (bit-identical sums; needs <= 4 dims per chunk and D <= 128).
+ *     Auto picks 2 when it fits.
+ *   GANN_OPT_PIVOT_WARPS: queries in flight per SM in mode 2 (8..24, 0 auto). */
+enum { GANN_OPT_ADC_MODE = 1, GANN_OPT_PIVOT_WARPS = 2 };
+int gann_set_option(gann_handle* h, int32_t option, int64_t value);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* gann_last_error(void);
 

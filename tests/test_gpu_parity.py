@@ -30,12 +30,18 @@ def _oracle(info, nav=True):
     return Oracle(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"] if nav else "", info["dtype"])
 
 
-@pytest.fixture(scope="module")
-def handles(index_root):
+@pytest.fixture(scope="module", params=["auto", "table"])
+def handles(index_root, request):
+    """Every index opened twice over the module: ADC mode auto (pivot-resident
+    wherever it fits) and forced per-query table mode."""
+    from gustann_b200.api import ADC_TABLE, GANN_OPT_ADC_MODE
     out = {}
     for name in INDEXES:
         info = get_index(index_root, name)
-        out[name] = (info, _open(info), _oracle(info))
+        g = _open(info)
+        if request.param == "table":
+            g.set_option(GANN_OPT_ADC_MODE, ADC_TABLE)
+        out[name] = (info, g, _oracle(info))
     yield out
     for _, g, o in out.values():
         g.close()
@@ -189,3 +195,21 @@ def test_reference_kernels_agree(handles, name):
         np.testing.assert_array_equal(rn[ok], nns[ok])
         np.testing.assert_array_equal(rd[ok], dist[ok])
     r.close()
+
+
+def test_pivot_mode_option(index_root):
+    from gustann_b200.api import ADC_PIVOT, ADC_TABLE, GANN_OPT_ADC_MODE, GANN_OPT_PIVOT_WARPS
+    info = get_index(index_root, "f32")
+    g = _open(info)
+    q = info["queries"][:300]
+    g.set_option(GANN_OPT_ADC_MODE, ADC_TABLE)
+    ref = g.query(q, 10, 48)
+    g.set_option(GANN_OPT_ADC_MODE, ADC_PIVOT)
+    for w in (8, 13, 24, 0):
+        g.set_option(GANN_OPT_PIVOT_WARPS, w)
+        out = g.query(q, 10, 48)
+        for u, v in zip(ref, out):
+            np.testing.assert_array_equal(u, v)
+    with pytest.raises(GustANNError):
+        g.set_option(GANN_OPT_PIVOT_WARPS, 7)
+    g.close()
