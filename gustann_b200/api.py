@@ -26,7 +26,8 @@ STATUS_NAMES = ["OK", "EINVAL", "EIO", "ENOMEM", "ECUDA", "ETIMEDOUT", "EUNSUPPO
 
 # Every symbol include/gann.h declares.
 EXPORTS = ["gann_open", "gann_open_device", "gann_search", "gann_search_device", "gann_close", "gann_last_error",
-           "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample", "gann_set_option"]
+           "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample", "gann_set_option",
+           "gann_search_noalloc"]
 GANN_OPT_ADC_MODE, GANN_OPT_PIVOT_WARPS = 1, 2
 ADC_AUTO, ADC_TABLE, ADC_PIVOT = 0, 1, 2
 
@@ -81,6 +82,7 @@ def _load() -> C.CDLL:
     lib.gann_probe_entry.argtypes = [vp, fp, i64, ip, ip]
     lib.gann_pivot_sample.argtypes = [i64, i64, C.c_uint32, ip]
     lib.gann_set_option.argtypes = [vp, i32, i64]
+    lib.gann_search_noalloc.argtypes = [C.POINTER(_DeviceIndex), vp, i64, i32, i32, vp, vp, vp, vp]
     for name in EXPORTS:
         if name != "gann_last_error":
             getattr(lib, name).restype = C.c_int

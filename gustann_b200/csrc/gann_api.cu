@@ -4,6 +4,7 @@
 #include <chrono>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <new>
 #include <numeric>
 #include <random>
@@ -574,3 +575,164 @@ int gann_pivot_sample(int64_t n, int64_t s, uint32_t seed, int32_t* out) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free search (gann_search_noalloc): every piece of library-side
+// device state of a call lives in this one static array, laid out per call as
+//   [0, 256)       work counter and error counters (cleared on every call)
+//   centroid       dim floats
+//   chunk offsets  pq_chunks + 1 int32
+//   raw pivots     256 x dim floats, copied from the caller's host array
+//   pivots_t       dim x 256 floats (transposed on the GPU)
+//   pivot table    pq_chunks x 256 float4 (only when chunks have <= 4 dims and dim <= 128)
+// Host code never uses the array's name as an address: the device address
+// comes from cudaGetSymbolAddress, looked up once per device.
+namespace {
+
+constexpr size_t kNoallocBytes = GANN_NOALLOC_SCRATCH_BYTES;
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocBytes];
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+__global__ void noalloc_stage_tables(const float* raw, const int32_t* off, int dim, int m, int with_piv,
+                                     float* pivots_t, float4* piv4) {
+  const int stride = gridDim.x * blockDim.x;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < dim * gann::kPivots; idx += stride) {
+    const int d = idx / gann::kPivots, j = idx % gann::kPivots;
+    pivots_t[idx] = raw[j * dim + d];
+  }
+  if (!with_piv) return;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < m * gann::kPivots; idx += stride) {
+    const int c = idx / gann::kPivots, j = idx % gann::kPivots;
+    const int a0 = off[c], a1 = off[c + 1];
+    float r[4];
+    for (int t = 0; t < 4; ++t) r[t] = a0 + t < a1 ? raw[j * dim + a0 + t] : 0.f;
+    piv4[idx] = make_float4(r[0], r[1], r[2], r[3]);
+  }
+}
+
+size_t noalloc_align(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+
+extern "C" int gann_search_noalloc(const gann_device_index* d, const float* d_queries, int64_t nq, int32_t topk,
+                                   int32_t ef_search, int32_t* d_nns, float* d_distances, int32_t* d_found_cnt,
+                                   void* stream) {
+  if (!d || !d->vectors || !d->adjacency || !d->codes || !d->pivots || !d->centroid || !d->chunk_offsets)
+    return set_error(GANN_EINVAL, "gann_search_noalloc: null array in the index descriptor");
+  if (d->dtype != GANN_UINT8 && d->dtype != GANN_FLOAT) return set_error(GANN_EINVAL, "gann_search_noalloc: bad dtype");
+  const int elem = d->dtype == GANN_UINT8 ? 1 : 4;
+  if (d->num_points <= 0 || d->num_points >= (int64_t(1) << 31) || d->dim <= 0 || d->dim > 1024)
+    return set_error(GANN_EINVAL, "gann_search_noalloc: bad index size");
+  if (d->max_degree < 1 || d->max_degree > 128 || d->adj_stride < d->max_degree || d->adj_stride % 4)
+    return set_error(GANN_EINVAL, "gann_search_noalloc: bad degree / adjacency stride");
+  if (d->vec_stride < d->dim * elem || d->vec_stride % 16 || d->code_stride % 16 || d->pq_chunks < 1 ||
+      d->pq_chunks > 128 || d->code_stride < d->pq_chunks)
+    return set_error(GANN_EINVAL, "gann_search_noalloc: bad row strides");
+  if (d->medoid < 0 || d->medoid >= d->num_points) return set_error(GANN_EINVAL, "gann_search_noalloc: bad medoid");
+  const uint32_t* off = d->chunk_offsets;
+  const int m = d->pq_chunks, dim = d->dim;
+  if (off[0] != 0 || off[m] != static_cast<uint32_t>(dim))
+    return set_error(GANN_EINVAL, "gann_search_noalloc: chunk offsets must span [0, dim]");
+  int maxw = 0;
+  bool all3 = true;
+  for (int i = 0; i < m; ++i) {
+    if (off[i + 1] <= off[i]) return set_error(GANN_EINVAL, "gann_search_noalloc: chunk offsets must increase");
+    maxw = std::max(maxw, static_cast<int>(off[i + 1] - off[i]));
+    all3 = all3 && off[i + 1] - off[i] == 3;
+  }
+  if (nq < 0 || nq >= (int64_t(1) << 31) - (int64_t(1) << 24))
+    return set_error(GANN_EINVAL, "gann_search_noalloc: query count out of range");
+  if (topk < 1 || topk > ef_search) return set_error(GANN_EINVAL, "gann_search_noalloc: need 1 <= topk <= ef_search");
+  if (ef_search > gann::search_max_ef())
+    return set_error(GANN_EUNSUPPORTED, "gann_search_noalloc: ef_search above " + std::to_string(gann::search_max_ef()));
+  if (nq > 0 && (!d_queries || !d_nns || !d_distances || !d_found_cnt))
+    return set_error(GANN_EINVAL, "gann_search_noalloc: null buffer");
+
+  // scratch layout for this index
+  const int piv_width = (maxw <= 4 && dim <= 128) ? (all3 ? 3 : 4) : 0;
+  size_t o = 256;
+  const size_t o_cen = o;
+  o = noalloc_align(o + sizeof(float) * dim);
+  const size_t o_off = o;
+  o = noalloc_align(o + sizeof(int32_t) * (m + 1));
+  const size_t o_raw = o;
+  o = noalloc_align(o + sizeof(float) * gann::kPivots * dim);
+  const size_t o_pt = o;
+  o = noalloc_align(o + sizeof(float) * gann::kPivots * dim);
+  const size_t o_piv = o;
+  if (piv_width) o = noalloc_align(o + sizeof(float4) * gann::kPivots * m);
+  if (o > kNoallocBytes)
+    return set_error(GANN_EUNSUPPORTED, "gann_search_noalloc: this index needs " + std::to_string(o) +
+                                            " bytes of scratch; the static scratch holds " +
+                                            std::to_string(kNoallocBytes));
+
+  if (d->device < 0 || d->device >= kNoallocMaxDevices)
+    return set_error(GANN_EUNSUPPORTED, "gann_search_noalloc: device ordinal outside 0..63");
+  GANN_CUDA(cudaSetDevice(d->device));
+  unsigned char* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[d->device]) {
+      void* p = nullptr;
+      GANN_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+      g_noalloc_ptr[d->device] = static_cast<unsigned char*>(p);
+    }
+    base = g_noalloc_ptr[d->device];
+  }
+  int sm_count = 0;
+  GANN_CUDA(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, d->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  // stage the small tables; the counters must start at zero
+  GANN_CUDA(cudaMemsetAsync(base, 0, 256, st));
+  GANN_CUDA(cudaMemcpyAsync(base + o_cen, d->centroid, sizeof(float) * dim, cudaMemcpyHostToDevice, st));
+  GANN_CUDA(cudaMemcpyAsync(base + o_off, off, sizeof(int32_t) * (m + 1), cudaMemcpyHostToDevice, st));
+  GANN_CUDA(cudaMemcpyAsync(base + o_raw, d->pivots, sizeof(float) * gann::kPivots * dim, cudaMemcpyHostToDevice, st));
+  noalloc_stage_tables<<<64, 256, 0, st>>>(reinterpret_cast<const float*>(base + o_raw),
+                                           reinterpret_cast<const int32_t*>(base + o_off), dim, m, piv_width > 0,
+                                           reinterpret_cast<float*>(base + o_pt),
+                                           reinterpret_cast<float4*>(base + o_piv));
+  GANN_CUDA(cudaGetLastError());
+
+  DeviceIndex ix;
+  ix.vecs = static_cast<const uint8_t*>(d->vectors);
+  ix.adj = d->adjacency;
+  ix.codes = d->codes;
+  ix.pivots_t = reinterpret_cast<const float*>(base + o_pt);
+  ix.centroid = reinterpret_cast<const float*>(base + o_cen);
+  ix.chunk_off = reinterpret_cast<const int32_t*>(base + o_off);
+  ix.n = d->num_points;
+  ix.dim = dim;
+  ix.degree = d->max_degree;
+  ix.chunks = m;
+  ix.vec_stride = d->vec_stride;
+  ix.adj_stride = d->adj_stride;
+  ix.code_stride = d->code_stride;
+  ix.medoid = d->medoid;
+  ix.has_nav = 0;
+  ix.piv4 = piv_width ? reinterpret_cast<const float4*>(base + o_piv) : nullptr;
+  ix.piv_width = piv_width;
+  int optin = 0;
+  GANN_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d->device));
+  if (gann::search_smem_bytes(ix, topk, ef_search) > static_cast<size_t>(optin))
+    return set_error(GANN_EUNSUPPORTED, "gann_search_noalloc: per-query working set exceeds shared memory");
+  if (nq == 0) return GANN_OK;
+
+  gann::SearchArgs a;
+  a.q = d_queries;
+  a.nq = nq;
+  a.topk = topk;
+  a.ef = ef_search;
+  a.max_hops = std::max(1 << 14, 64 * ef_search);
+  a.nav_max_hops = 1 << 20;
+  a.nns = d_nns;
+  a.dist = d_distances;
+  a.found = d_found_cnt;
+  a.qcounter = reinterpret_cast<int32_t*>(base);
+  a.err = reinterpret_cast<int32_t*>(base) + 1;
+  GANN_CUDA(gann::launch_search(ix, a, d->dtype, sm_count, st));
+  return GANN_OK;
+}

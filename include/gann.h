@@ -153,6 +153,32 @@ typedef struct {
 
 int gann_open_device(const gann_device_index* desc, gann_handle** out);
 
+/*
+ * Allocation-free search. For callers that cannot call cudaMalloc on the
+ * search path -- a serving process whose HBM is handed out by another runtime's
+ * arena, or a caller that must not trigger the allocator's device-wide
+ * synchronisation while other work is in flight. It searches the caller-owned
+ * device index described by `desc` (the gann_open_device layout) for queries
+ * and outputs the caller also owns, and allocates nothing: the library-side
+ * device state of the call -- the work and error counters, and the centroid,
+ * chunk offsets and PQ pivot tables staged from desc's host arrays -- lives in
+ * one static device array of GANN_NOALLOC_SCRATCH_BYTES (1 MiB) that every GPU
+ * loading the library holds until exit. The table space needed is about
+ * 2048*dim + 4096*pq_chunks bytes; an index needing more than the array is
+ * rejected with GANN_EUNSUPPORTED. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture. All calls share the one array and each call re-stages
+ * it, so calls whose work overlaps on the GPU race: serialise them (one stream,
+ * or wait for the previous call). Asynchronous on `stream`; results are the
+ * same as gann_search_device over the same arrays.
+ * No counterpart in the reference, which allocates per search call
+ * (src/pure_mem.cu:78-89).
+ */
+#define GANN_NOALLOC_SCRATCH_BYTES (1u << 20)
+int gann_search_noalloc(const gann_device_index* desc, const float* d_queries, int64_t nq,
+                        int32_t topk, int32_t ef_search, int32_t* d_nns, float* d_distances,
+                        int32_t* d_found_cnt, void* stream);
+
 /* Release device and host memory of the handle (GustANN::~GustANN,
  * src/ssd_search.cu:112-137). NULL is accepted. */
 int gann_close(gann_handle* h);
