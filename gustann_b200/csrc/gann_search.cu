@@ -269,9 +269,17 @@ struct WarpSmem {
   uint64_t* cand;
   int* candr;
   int* hist;
+  uint32_t* filt;   // lossy id -> pool-membership table (see traverse)
   float* topd;
   int* topi;
 };
+
+// Pool-membership table size: a power of two >= the pool capacity.
+__host__ __device__ inline int filt_bits(int pl) {
+  int b = 5;
+  while ((1 << b) < pl * kWarp) ++b;
+  return b;
+}
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
@@ -293,6 +301,7 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
   unsigned char* cand = take(sizeof(uint64_t) * npl * kWarp);
   unsigned char* candr = take(sizeof(int) * npl * kWarp);
   unsigned char* hist = take(sizeof(int) * (pl * kWarp + kWarp));
+  unsigned char* filt = take(sizeof(uint32_t) << filt_bits(pl));
   unsigned char* topd = take(sizeof(float) * topk);
   unsigned char* topi = take(sizeof(int) * topk);
   if (w) {
@@ -304,6 +313,7 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
     w->cand = reinterpret_cast<uint64_t*>(cand);
     w->candr = reinterpret_cast<int*>(candr);
     w->hist = reinterpret_cast<int*>(hist);
+    w->filt = reinterpret_cast<uint32_t*>(filt);
     w->topd = reinterpret_cast<float*>(topd);
     w->topi = reinterpret_cast<int*>(topi);
   }
@@ -336,16 +346,26 @@ __device__ __forceinline__ void load_node(const DeviceIndex& ix, uint32_t u, int
 // pool -- so it is known right after the ADC step. Its record is requested
 // then, and the merge and the top-k insert of the current node run while that
 // load is in flight.
-template <typename T, int NPL, int PL, int VP, int PIV>
+//
+// A neighbour that is already in the pool would be dropped as a duplicate of
+// the pool copy (same id, hence same PQ distance), so its code row and ADC are
+// skipped when the membership table says so. The table is lossy but never
+// wrong in that direction: slot h(id) holds id only while id is in the pool
+// (written when it enters, cleared when it is pushed out past `ef`).
+template <typename T, int NPL, int VP, int PIV>
 __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid, uint32_t entry,
-                         const WarpSmem& s, const float4* __restrict__ piv, int lane) {
+                         const WarpSmem& s, const float4* __restrict__ piv, int lane, int pl) {
   const int dim = ix.dim, M = ix.chunks, L = a.ef, topk = a.topk;
   const int mw = ix.code_stride >> 4;
-  int psize = 0, tcnt = 0;
+  const int fbits = filt_bits(pl);
+  const int fsz = 1 << fbits;
+  auto fslot = [fbits](uint32_t id) { return static_cast<int>((id * 0x9E3779B1u) >> (32 - fbits)); };
+  int psize = 0, tcnt = 0, pfirst = 0;
   uint32_t hops = 0, adc = 0;
   uint32_t u = entry;
   bool capped = false;
 
+  for (int i = lane; i < fsz; i += kWarp) s.filt[i] = kPadId;
   float qv[VP];   // q'' = (q - c) + c, the lane's dims
 #pragma unroll
   for (int v = 0; v < VP; ++v) {
@@ -355,6 +375,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
   uint32_t nb[NPL];
   float xv[VP];
   load_node<T, NPL, VP>(ix, u, lane, nb, xv);
+  __syncwarp();
 
   for (;;) {
     if (hops >= static_cast<uint32_t>(a.max_hops)) {
@@ -367,15 +388,15 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     uint4 cur[NPL];
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
-      ok[k] = nb[k] != kPadId;
+      adc += __popc(__ballot_sync(kFull, nb[k] != kPadId));
+      ok[k] = nb[k] != kPadId && s.filt[fslot(nb[k])] != nb[k];
       crow[k] = reinterpret_cast<const uint4*>(ix.codes + static_cast<size_t>(ok[k] ? nb[k] : 0) * ix.code_stride);
       cur[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
     }
 
-    // first unvisited pool entry (the pool is as the last merge left it)
+    // first unvisited pool entry; every entry before `pfirst` is visited
     int ppos = -1;
-#pragma unroll
-    for (int j = 0; j < PL; ++j) {
+    for (int j = pfirst >> 5; kWarp * j < psize; ++j) {
       const int i = lane + kWarp * j;
       const unsigned bm = __ballot_sync(kFull, i < psize && (s.pool[i] & 1ull));
       if (bm) {
@@ -383,9 +404,11 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
         break;
       }
     }
+    pfirst = ppos >= 0 ? ppos : psize;
     const uint64_t pstar = ppos >= 0 ? s.pool[ppos] : ~0ull;
 
-    // ADC of every neighbour, one lane per neighbour, chunks in order
+    // ADC of every neighbour not known to be in the pool, one lane per
+    // neighbour, chunks in order
     float dsum[NPL];
 #pragma unroll
     for (int k = 0; k < NPL; ++k) dsum[k] = 0.f;
@@ -420,7 +443,6 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     uint64_t mk = ~0ull;
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
-      adc += __popc(__ballot_sync(kFull, ok[k]));
       key[k] = make_key(dsum[k], nb[k]);
       rk[k] = 0;
       if (ok[k]) {
@@ -517,6 +539,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       // final slot of each survivor = rank in pool + rank among survivors
       uint64_t ck[NPL];
       int cpos[NPL], cr[NPL];
+      int rmin = INT_MAX;
 #pragma unroll
       for (int k = 0; k < NPL; ++k) {
         const int si = lane + kWarp * k;
@@ -534,20 +557,22 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
           }
           cpos[k] = cr[k] + less;
           if (ck[k] == nxt) ck[k] &= ~1ull;
+          rmin = min(rmin, cr[k]);
         }
       }
-      // pool entry i moves right by the number of survivors ranked <= i
-      for (int i = lane; i <= psize; i += kWarp) s.hist[i] = 0;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) rmin = min(rmin, __shfl_xor_sync(kFull, rmin, off));
+      // entries before rmin stay; entry i >= rmin moves right by the number of
+      // survivors ranked <= i (histogram of ranks, then a prefix sum)
+      const int j0 = rmin >> 5;
+      for (int i = kWarp * j0 + lane; i <= psize; i += kWarp) s.hist[i] = 0;
       __syncwarp();
 #pragma unroll
       for (int k = 0; k < NPL; ++k)
         if (lane + kWarp * k < S) atomicAdd(&s.hist[cr[k]], 1);
       __syncwarp();
-      uint64_t pv[PL];
-      int pd[PL];
       int carry = 0;
-#pragma unroll
-      for (int j = 0; j < PL; ++j) {
+      for (int j = j0; kWarp * j < psize; ++j) {
         const int i = lane + kWarp * j;
         int h = i < psize ? s.hist[i] : 0;
 #pragma unroll
@@ -555,23 +580,43 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
           const int y = __shfl_up_sync(kFull, h, off);
           if (lane >= off) h += y;
         }
-        pd[j] = INT_MAX;
-        pv[j] = 0;
-        if (i < psize) {
-          pv[j] = s.pool[i];
-          if (pv[j] == nxt) pv[j] &= ~1ull;
-          pd[j] = i + h + carry;
-        }
+        if (i < psize) s.hist[i] = h + carry;
         carry += __shfl_sync(kFull, h, kWarp - 1);
       }
       __syncwarp();
+      // moves, last chunk first (an entry only moves right); entries pushed
+      // past `ef` leave the pool and the membership table
+      for (int j = (psize - 1) >> 5; j >= j0; --j) {
+        const int i = lane + kWarp * j;
+        uint64_t v = 0;
+        int dst = INT_MAX;
+        if (i < psize) {
+          v = s.pool[i];
+          dst = i + s.hist[i];
+          if (v == nxt) v &= ~1ull;
+        }
+        __syncwarp();
+        if (i < psize) {
+          if (dst < L) {
+            s.pool[dst] = v;
+          } else {
+            const uint32_t id = static_cast<uint32_t>(v) >> 1;
+            const int sl = fslot(id);
+            if (s.filt[sl] == id) s.filt[sl] = kPadId;
+          }
+        }
+        __syncwarp();
+      }
 #pragma unroll
-      for (int j = 0; j < PL; ++j)
-        if (pd[j] < L) s.pool[pd[j]] = pv[j];
-#pragma unroll
-      for (int k = 0; k < NPL; ++k)
-        if (cpos[k] < L) s.pool[cpos[k]] = ck[k];
+      for (int k = 0; k < NPL; ++k) {
+        if (cpos[k] < L) {
+          s.pool[cpos[k]] = ck[k];
+          const uint32_t id = static_cast<uint32_t>(ck[k]) >> 1;
+          s.filt[fslot(id)] = id;
+        }
+      }
       psize = min(psize + S, L);
+      pfirst = min(pfirst, rmin);
     } else if (more && lane == 0) {
       s.pool[ppos] = pstar & ~1ull;   // no survivor: the next node is pool entry ppos
     }
@@ -600,9 +645,9 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
 }
 
 // One query per warp, from query setup to the written top-k.
-template <typename T, int NPL, int PL, int VP, int PIV>
+template <typename T, int NPL, int VP, int PIV>
 __device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchArgs& a, const WarpSmem& s,
-                                            const float4* __restrict__ piv, int lane) {
+                                            const float4* __restrict__ piv, int lane, int pl) {
   const int dim = ix.dim;
   for (;;) {
     int qid = 0;
@@ -641,27 +686,27 @@ __device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchA
       }
     }
     __syncwarp();
-    traverse<T, NPL, PL, VP, PIV>(ix, a, qid, entry, s, piv, lane);
+    traverse<T, NPL, VP, PIV>(ix, a, qid, entry, s, piv, lane, pl);
     __syncwarp();
   }
 }
 
 // Table mode: one warp per CTA, the warp's ADC table in its shared memory.
-template <typename T, int NPL, int PL, int VP>
-__global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, const SearchArgs a) {
+template <typename T, int NPL, int VP>
+__global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, const SearchArgs a, int pl) {
   extern __shared__ __align__(16) unsigned char smem[];
   WarpSmem s;
-  carve(smem, ix.chunks, ix.dim, NPL, PL, a.topk, &s, false);
-  run_queries<T, NPL, PL, VP, 0>(ix, a, s, nullptr, threadIdx.x);
+  carve(smem, ix.chunks, ix.dim, NPL, pl, a.topk, &s, false);
+  run_queries<T, NPL, VP, 0>(ix, a, s, nullptr, threadIdx.x, pl);
 }
 
 // Pivot mode: one persistent CTA per SM holds the 256 x D pivot table once
 // (M x 4 KB) and runs up to kPivWarps queries at a time, one per warp, each
-// with ~2-8 KB of private state instead of a 4*M KB table.
+// with a few KB of private state instead of a 4*M KB table.
 constexpr int kPivWarps = 24;
-template <typename T, int NPL, int PL, int VP, int CW>
+template <typename T, int NPL, int VP, int CW>
 __global__ void __launch_bounds__(kWarp * kPivWarps, 1) search_kernel_piv(const DeviceIndex ix, const SearchArgs a,
-                                                                          size_t per_warp) {
+                                                                          size_t per_warp, int pl) {
   extern __shared__ __align__(16) unsigned char smem[];
   float4* piv = reinterpret_cast<float4*>(smem);
   const int ntab = ix.chunks * kPivots;
@@ -669,8 +714,8 @@ __global__ void __launch_bounds__(kWarp * kPivWarps, 1) search_kernel_piv(const 
   __syncthreads();
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   WarpSmem s;
-  carve(smem + sizeof(float4) * ntab + per_warp * warp, ix.chunks, ix.dim, NPL, PL, a.topk, &s, true);
-  run_queries<T, NPL, PL, VP, CW>(ix, a, s, piv, lane);
+  carve(smem + sizeof(float4) * ntab + per_warp * warp, ix.chunks, ix.dim, NPL, pl, a.topk, &s, true);
+  run_queries<T, NPL, VP, CW>(ix, a, s, piv, lane, pl);
 }
 
 template <typename T>
@@ -710,34 +755,36 @@ __global__ void __launch_bounds__(kWarp) probe_entry_kernel(const DeviceIndex ix
 }
 
 int npl_for(int degree) { return degree <= 64 ? 2 : 4; }
-int pl_for(int ef) { return ef <= 64 ? 2 : ef <= 128 ? 4 : ef <= 256 ? 8 : 16; }
+int pl_for(int ef) { return (ef + kWarp - 1) / kWarp; }
 int vp_for(int dim) { return dim <= 128 ? 4 : 32; }
 
-template <typename T, int NPL, int PL, int VP>
+template <typename T, int NPL, int VP>
 cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const int pl = pl_for(a.ef);
   if constexpr (VP == 4) if (ix.piv_width > 0 && ix.adc_mode != 1) {
     // pivot mode when the table plus at least 8 warps' state fit (dims <= 128;
     // wider vectors have too many chunks for a shared-memory pivot table)
     const size_t tab = sizeof(float4) * ix.chunks * kPivots;
-    const size_t per_warp = carve(nullptr, ix.chunks, ix.dim, NPL, PL, a.topk, nullptr, true);
-    int warps = static_cast<int>(std::min<size_t>(kPivWarps, (optin - tab) / per_warp));
+    const size_t per_warp = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, true);
+    int warps = tab < static_cast<size_t>(optin)
+                    ? static_cast<int>(std::min<size_t>(kPivWarps, (optin - tab) / per_warp)) : 0;
     if (ix.piv_warps > 0) warps = std::min(warps, ix.piv_warps);
-    if (tab < static_cast<size_t>(optin) && warps >= 8) {
+    if (warps >= 8) {
       const size_t smem = tab + per_warp * warps;
-      auto fn = ix.piv_width == 3 ? search_kernel_piv<T, NPL, PL, VP, 3> : search_kernel_piv<T, NPL, PL, VP, 4>;
+      auto fn = ix.piv_width == 3 ? search_kernel_piv<T, NPL, VP, 3> : search_kernel_piv<T, NPL, VP, 4>;
       cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (e != cudaSuccess) return e;
       int64_t grid = std::min<int64_t>(sm_count, (a.nq + warps - 1) / warps);
       if (grid <= 0) return cudaSuccess;
-      fn<<<static_cast<unsigned>(grid), kWarp * warps, smem, st>>>(ix, a, per_warp);
+      fn<<<static_cast<unsigned>(grid), kWarp * warps, smem, st>>>(ix, a, per_warp, pl);
       return cudaGetLastError();
     }
   }
-  const size_t smem = carve(nullptr, ix.chunks, ix.dim, NPL, PL, a.topk, nullptr, false);
-  auto fn = search_kernel<T, NPL, PL, VP>;
+  const size_t smem = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, false);
+  auto fn = search_kernel<T, NPL, VP>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   int per_sm = 0;
@@ -747,19 +794,14 @@ cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_co
   int64_t grid = static_cast<int64_t>(per_sm) * sm_count;
   if (grid > a.nq) grid = a.nq;
   if (grid <= 0) return cudaSuccess;
-  fn<<<static_cast<unsigned>(grid), kWarp, smem, st>>>(ix, a);
+  fn<<<static_cast<unsigned>(grid), kWarp, smem, st>>>(ix, a, pl);
   return cudaGetLastError();
 }
 
 template <typename T, int VP>
 cudaError_t launch_vp(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
-  const int npl = npl_for(ix.degree), pl = pl_for(a.ef);
-#define GANN_CASE(N, P) \
-  if (npl == N && pl == P) return launch_variant<T, N, P, VP>(ix, a, sm_count, st);
-  GANN_CASE(2, 2) GANN_CASE(2, 4) GANN_CASE(2, 8) GANN_CASE(2, 16)
-  GANN_CASE(4, 2) GANN_CASE(4, 4) GANN_CASE(4, 8) GANN_CASE(4, 16)
-#undef GANN_CASE
-  return cudaErrorInvalidValue;
+  if (npl_for(ix.degree) == 2) return launch_variant<T, 2, VP>(ix, a, sm_count, st);
+  return launch_variant<T, 4, VP>(ix, a, sm_count, st);
 }
 
 template <typename T>
@@ -770,7 +812,7 @@ cudaError_t launch_typed(const DeviceIndex& ix, const SearchArgs& a, int sm_coun
 
 }  // namespace
 
-int search_max_ef() { return 16 * kWarp; }
+int search_max_ef() { return 32 * kWarp; }
 
 int make_pivot_table(const std::vector<float>& pivots_t, const std::vector<int32_t>& chunk_off, int dim,
                      std::vector<float>& out) {

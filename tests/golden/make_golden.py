@@ -63,6 +63,11 @@ def make_ref(out: str) -> None:
         p = paths(name)
         q = np.load(os.path.join(HERE, name, "queries.npy"))
         dtype = 0 if kind == "sift" else 1
+        # the reference only gets inputs inside its defined behaviour
+        from oracle import Oracle
+        o = Oracle(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"], dtype)
+        for ef in EFS:
+            assert not o.search(q, TOPK, ef)[4].any(), "golden queries must be flag-free"
         r = RefGPU(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"], dtype, dim)
         res = {"lut": r.lut(q[:8], M)}
         res["nav_sample"], res["nav_entry"] = r.nav(q)

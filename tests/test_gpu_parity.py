@@ -14,7 +14,7 @@ from oracle import F_DUPNBR, F_HOPCAP, F_NAVRACE, F_STALE, Oracle, RefGPU
 
 pytestmark = pytest.mark.gpu
 
-EFS = [10, 33, 64, 100, 200]
+EFS = [10, 33, 64, 100, 200, 480, 1000]
 
 
 def _open(info, use_gpu_mem=True, nav=True):
@@ -173,27 +173,35 @@ def test_bad_arguments_raise(handles):
 @pytest.mark.skipif(not RefGPU.available(), reason="reference library not built")
 @pytest.mark.parametrize("name", list(INDEXES))
 def test_reference_kernels_agree(handles, name):
-    """The reference's own compiled kernels on the B200, same files and queries."""
+    """The reference's own compiled kernels on the B200, same files and queries.
+
+    The reference is handed only queries the oracle shows to be inside its
+    defined behaviour at that ef (flags == 0): on the others it would expand a
+    pool slot it never wrote or index its pivot map out of range, which can
+    read outside its buffers. Queries are independent there (one CTA each), so
+    dropping them changes nothing for the rest."""
     info, g, o = handles[name]
     p = info["paths"]
     r = RefGPU(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"], info["dtype"], info["dim"])
     q = info["queries"][:200]
     np.testing.assert_array_equal(r.lut(q[:32], info["M"]), g.probe_lut(q[:32]))
     if p["nav_graph_prefix"]:
-        rs, re = r.nav(q)
-        s, e = g.probe_entry(q)
-        _, _, of = o.nav(q)
-        ok = (of & F_NAVRACE) == 0
-        np.testing.assert_array_equal(rs[ok], s[ok])
-        np.testing.assert_array_equal(re[ok], e[ok])
-    for ef in (10, 64, 200):
-        rn, rd, rf, _ = r.search(q, 10, ef)
-        nns, dist, found = g.query(q, 10, ef)
-        _, _, _, _, of = o.search(q, 10, ef)
-        ok = of == 0
-        np.testing.assert_array_equal(rf[ok], found[ok])
-        np.testing.assert_array_equal(rn[ok], nns[ok])
-        np.testing.assert_array_equal(rd[ok], dist[ok])
+        os_, _, of = o.nav(q)
+        s_cnt = len(np.loadtxt(p["nav_graph_prefix"] + "/map.txt", ndmin=1))
+        clean = ((of & F_NAVRACE) == 0) & (os_ >= 0) & (os_ < s_cnt)
+        rs, re = r.nav(q[clean])
+        s, e = g.probe_entry(q[clean])
+        np.testing.assert_array_equal(rs, s)
+        np.testing.assert_array_equal(re, e)
+    for ef in (10, 64, 200, 700):
+        of = o.search(q, 10, ef)[4]
+        qc = q[of == 0]
+        assert len(qc) > len(q) // 2
+        rn, rd, rf, _ = r.search(qc, 10, ef)
+        nns, dist, found = g.query(qc, 10, ef)
+        np.testing.assert_array_equal(rf, found)
+        np.testing.assert_array_equal(rn, nns)
+        np.testing.assert_array_equal(rd, dist)
     r.close()
 
 
