@@ -615,6 +615,9 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
           s.filt[fslot(id)] = id;
         }
       }
+      // a next node taken from the pool in front of every survivor keeps its
+      // slot and was not rewritten by the moves above: mark it here
+      if (nxt == pstar && ppos < kWarp * j0 && lane == 0) s.pool[ppos] = pstar & ~1ull;
       psize = min(psize + S, L);
       pfirst = min(pfirst, rmin);
     } else if (more && lane == 0) {
