@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--n", type=int, default=0, help="override the number of base points")
     ap.add_argument("--nq", type=int, default=10000)
     ap.add_argument("--target", type=float, default=0.9)
-    ap.add_argument("--efs", default="32,64,96,128,192,256,320,384,448,512,640,768,896,1024")
+    ap.add_argument("--efs", default="32,48,64,80,96,112,128,144,160,176,192,224,256,320,384,448,512,640,768,1024")
     ap.add_argument("--cache", default=os.environ.get("GANN_BENCH_CACHE", "/tmp/gann_bench"))
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -172,7 +172,7 @@ def traffic_per_launch(cfg_key: str):
 
 # ------------------------------------------------------------------ data
 def ensure_index(spec, args, d: Dist) -> dict:
-    key = f"{args.config}_n{spec.n}_R64_M32_v2"
+    key = f"{args.config}_n{spec.n}_R64_M32_v3"
     root = os.path.join(args.cache, key)
     done = os.path.join(root, "DONE")
     paths = formats.index_paths(root)

@@ -268,7 +268,7 @@ struct WarpSmem {
   uint64_t* pool;
   uint64_t* cand;
   int* candr;
-  int* hist;
+  int* hist;       // survivor ranks in key order (merge)
   uint32_t* filt;   // lossy id -> pool-membership table (see traverse)
   float* topd;
   int* topi;
@@ -300,7 +300,7 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
   unsigned char* pool = take(sizeof(uint64_t) * pl * kWarp);
   unsigned char* cand = take(sizeof(uint64_t) * npl * kWarp);
   unsigned char* candr = take(sizeof(int) * npl * kWarp);
-  unsigned char* hist = take(sizeof(int) * (pl * kWarp + kWarp));
+  unsigned char* hist = take(sizeof(int) * ((pl > npl ? pl : npl) * kWarp + kWarp));
   unsigned char* filt = take(sizeof(uint32_t) << filt_bits(pl));
   unsigned char* topd = take(sizeof(float) * topk);
   unsigned char* topi = take(sizeof(int) * topk);
@@ -562,45 +562,38 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) rmin = min(rmin, __shfl_xor_sync(kFull, rmin, off));
-      // entries before rmin stay; entry i >= rmin moves right by the number of
-      // survivors ranked <= i (histogram of ranks, then a prefix sum)
-      const int j0 = rmin >> 5;
-      for (int i = kWarp * j0 + lane; i <= psize; i += kWarp) s.hist[i] = 0;
-      __syncwarp();
+      // survivor ranks in key order are non-decreasing: hist[t] = rank of the
+      // t-th smallest survivor; entry i >= rmin moves right by #{t : hist[t] <= i}
 #pragma unroll
       for (int k = 0; k < NPL; ++k)
-        if (lane + kWarp * k < S) atomicAdd(&s.hist[cr[k]], 1);
+        if (lane + kWarp * k < S) s.hist[cpos[k] - cr[k]] = cr[k];
       __syncwarp();
-      int carry = 0;
-      for (int j = j0; kWarp * j < psize; ++j) {
-        const int i = lane + kWarp * j;
-        int h = i < psize ? s.hist[i] : 0;
+      // moves, four chunks at a time from the last one down (an entry only moves
+      // right); entries pushed past `ef` leave the pool and the membership table
+      const int j0 = rmin >> 5;
+      for (int jg = (psize - 1) >> 5; jg >= j0; jg -= 4) {
+        uint64_t v[4];
+        int dst[4];
 #pragma unroll
-        for (int off = 1; off < kWarp; off <<= 1) {
-          const int y = __shfl_up_sync(kFull, h, off);
-          if (lane >= off) h += y;
-        }
-        if (i < psize) s.hist[i] = h + carry;
-        carry += __shfl_sync(kFull, h, kWarp - 1);
-      }
-      __syncwarp();
-      // moves, last chunk first (an entry only moves right); entries pushed
-      // past `ef` leave the pool and the membership table
-      for (int j = (psize - 1) >> 5; j >= j0; --j) {
-        const int i = lane + kWarp * j;
-        uint64_t v = 0;
-        int dst = INT_MAX;
-        if (i < psize) {
-          v = s.pool[i];
-          dst = i + s.hist[i];
-          if (v == nxt) v &= ~1ull;
+        for (int g = 0; g < 4; ++g) {
+          const int i = lane + kWarp * (jg - g);
+          dst[g] = INT_MAX;
+          v[g] = 0;
+          if (jg - g >= j0 && i < psize) {
+            v[g] = s.pool[i];
+            int t = 0;
+            while (t < S && s.hist[t] <= i) ++t;
+            dst[g] = i + t;
+            if (v[g] == nxt) v[g] &= ~1ull;
+          }
         }
         __syncwarp();
-        if (i < psize) {
-          if (dst < L) {
-            s.pool[dst] = v;
-          } else {
-            const uint32_t id = static_cast<uint32_t>(v) >> 1;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          if (dst[g] < L) {
+            s.pool[dst[g]] = v[g];
+          } else if (dst[g] != INT_MAX) {
+            const uint32_t id = static_cast<uint32_t>(v[g]) >> 1;
             const int sl = fslot(id);
             if (s.filt[sl] == id) s.filt[sl] = kPadId;
           }

@@ -43,7 +43,7 @@ def sample_pivots(n: int, s: int) -> np.ndarray:
 def build_index(root: str, X: torch.Tensor, dtype: int, R: int = 64, alpha: float = 1.2, M: int = 32,
                 nav_samples: int = 1_000_000, nav: bool = True, seed: int = 0, verbose: bool = False,
                 pq_legacy: bool = False, long_range: int = 4, L_build: int = 100, nav_L: int = 50,
-                builder: str = "auto", passes: int = 1) -> dict:
+                builder: str = "auto", passes: int = 2) -> dict:
     """Build every index file under ``root`` for base vectors ``X`` [N, D].
 
     ``builder``: "vamana" (GPU; greedy-search candidates, the construction the
