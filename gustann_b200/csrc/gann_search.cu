@@ -218,32 +218,30 @@ __device__ __forceinline__ void build_lut(const DeviceIndex& ix, const float* __
   }
 }
 
-// Sum LUT entries for up to 16 codes packed in `c`, in chunk order.
-__device__ __forceinline__ float adc16(float s, const uint4 c, const float* __restrict__ lut, int n) {
-  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-  for (int b = 0; b < 16; ++b) {
-    if (b < n) s = __fadd_rn(s, lut[b * kPivots + ((w[b >> 2] >> (8 * (b & 3))) & 0xffu)]);
-  }
-  return s;
-}
-
-// The same sums without a per-query table: the table entry of chunk `b` and
+// ADC without a per-query table (pivot mode): the table entry of chunk `b` and
 // code `j` is recomputed from the CTA-resident pivot row piv[b][j] (zero-padded
 // to 4 dims) and the query residual qcp[b] -- d = qc_i - p_ji, e = fma(d, d, e)
 // from 0 over the chunk's dims in order, then s += e -- which are the fp32
 // operations that produce and consume the reference's table entry, so the sum
 // is bit-identical. CW = dims per chunk (4 also serves mixed widths <= 4: the
 // zero padding contributes fma(0, 0, e) = e).
-template <int CW>
-__device__ __forceinline__ float adc16_piv(float s, const uint4 c, const float4* __restrict__ piv,
-                                           const float4* __restrict__ qcp, int n) {
-  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+
+// Four chunks at a time (one 32-bit word of codes), for the early exit below.
+__device__ __forceinline__ float adc4(float s, uint32_t w, const float* __restrict__ lut, int n) {
 #pragma unroll
-  for (int b = 0; b < 16; ++b) {
+  for (int b = 0; b < 4; ++b)
+    if (b < n) s = __fadd_rn(s, lut[b * kPivots + ((w >> (8 * b)) & 0xffu)]);
+  return s;
+}
+
+template <int CW>
+__device__ __forceinline__ float adc4_piv(float s, uint32_t w, const float4* __restrict__ piv,
+                                          const float4* __restrict__ qcp, int n) {
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
     if (b < n) {
       const float4 q = qcp[b];
-      const float4 p = piv[b * kPivots + ((w[b >> 2] >> (8 * (b & 3))) & 0xffu)];
+      const float4 p = piv[b * kPivots + ((w >> (8 * b)) & 0xffu)];
       float d = __fsub_rn(q.x, p.x);
       float e = __fmul_rn(d, d);
       d = __fsub_rn(q.y, p.y);
@@ -258,6 +256,12 @@ __device__ __forceinline__ float adc16_piv(float s, const uint4 c, const float4*
     }
   }
   return s;
+}
+
+// Distance held in a pool key (inverse of ord_f32).
+__device__ __forceinline__ float key_dist(uint64_t key) {
+  const uint32_t o = static_cast<uint32_t>(key >> 32);
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
 }
 
 struct WarpSmem {
@@ -408,32 +412,61 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     const uint64_t pstar = ppos >= 0 ? s.pool[ppos] : ~0ull;
 
     // ADC of every neighbour not known to be in the pool, one lane per
-    // neighbour, chunks in order
+    // neighbour, chunks in order. With a full pool a neighbour whose partial
+    // sum already exceeds the last entry's distance is settled: table entries
+    // are >= 0 and round-to-nearest sums of them never decrease, so its final
+    // key lies beyond the last entry and the merge would drop it -- its
+    // remaining chunks are skipped, and the warp leaves once no lane is live.
     float dsum[NPL];
+    bool live[NPL];
 #pragma unroll
-    for (int k = 0; k < NPL; ++k) dsum[k] = 0.f;
+    for (int k = 0; k < NPL; ++k) {
+      dsum[k] = 0.f;
+      live[k] = ok[k];
+    }
+    const bool full = psize == L;
+    const float lastd = full ? key_dist(s.pool[L - 1]) : INFINITY;
     for (int w = 0; w < mw; ++w) {
       uint4 nxt[NPL];
       const bool more = w + 1 < mw;
 #pragma unroll
-      for (int k = 0; k < NPL; ++k) nxt[k] = (more && ok[k]) ? __ldg(crow[k] + w + 1) : make_uint4(0, 0, 0, 0);
+      for (int k = 0; k < NPL; ++k) nxt[k] = (more && live[k]) ? __ldg(crow[k] + w + 1) : make_uint4(0, 0, 0, 0);
       const int n = min(16, M - 16 * w);
-      if (PIV == 0) {
-        const float* lw = s.lut + 16 * w * kPivots;
+      bool any = true;
 #pragma unroll
-        for (int k = 0; k < NPL; ++k)
-          if (ok[k]) dsum[k] = adc16(dsum[k], cur[k], lw, n);
-      } else {
-        const float4* pw = piv + 16 * w * kPivots;
-        const float4* qw = s.qcp + 16 * w;
+      for (int sub = 0; sub < 4; ++sub) {
+        const int nc = n - 4 * sub;
+        if (nc <= 0) break;
 #pragma unroll
-        for (int k = 0; k < NPL; ++k)
-          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3>(dsum[k], cur[k], pw, qw, n)
-                                        : adc16_piv<4>(dsum[k], cur[k], pw, qw, n);
+        for (int k = 0; k < NPL; ++k) {
+          if (live[k]) {
+            const uint32_t wd = sub == 0 ? cur[k].x : sub == 1 ? cur[k].y : sub == 2 ? cur[k].z : cur[k].w;
+            const int c0 = 16 * w + 4 * sub;
+            if (PIV == 0)
+              dsum[k] = adc4(dsum[k], wd, s.lut + c0 * kPivots, nc);
+            else if (PIV == 3)
+              dsum[k] = adc4_piv<3>(dsum[k], wd, piv + c0 * kPivots, s.qcp + c0, nc);
+            else
+              dsum[k] = adc4_piv<4>(dsum[k], wd, piv + c0 * kPivots, s.qcp + c0, nc);
+          }
+        }
+        if (full) {
+          bool l = false;
+#pragma unroll
+          for (int k = 0; k < NPL; ++k) {
+            live[k] = live[k] && !(dsum[k] > lastd);
+            l = l || live[k];
+          }
+          any = __any_sync(kFull, l);
+          if (!any) break;
+        }
       }
 #pragma unroll
       for (int k = 0; k < NPL; ++k) cur[k] = nxt[k];
+      if (!any) break;
     }
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) ok[k] = ok[k] && live[k];
 
     // candidates that can enter the pool: not beyond its last entry when full,
     // not already in it; rank = insertion point (lower bound on (dist, id))
