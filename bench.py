@@ -234,7 +234,11 @@ def cpu_baseline(paths, dtype, Q, ef, seconds):
 
 def run_reference(args, d: Dist):
     """--impl reference: the reference path's CPU restatement (the reference
-    has no CPU search of its own) timed on the host cores; rank 0 only."""
+    has no CPU search of its own) timed on the host cores; rank 0 only.
+
+    Also reported, as context: the reference's own CUDA kernels (compiled from
+    its sources into oracle/_ref) on this GPU, same index, queries and ef --
+    given only the queries the oracle shows inside its defined behaviour."""
     if d.rank != 0:
         return
     spec = spec_for(args)
@@ -247,20 +251,19 @@ def run_reference(args, d: Dist):
     o = orc.Oracle(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], spec.dtype)
     cores = os.cpu_count() or 1
     efs = [int(x) for x in args.efs.split(",")]
-    probe = min(1000, len(Q))
-    ef, rec = efs[-1], 0.0
+    ef, rec, flags = efs[-1], 0.0, None
     for e in efs:
-        nns = o.search(Q[:probe], TOPK, e, threads=cores)[0]
-        rec = recall_at(nns, gt[:probe])
+        nns, _, _, _, fl = o.search(Q, TOPK, e, threads=cores)
+        rec, flags = recall_at(nns, gt), fl
         if rec >= args.target:
             ef = e
             break
-    per_step = max(1, int(min(len(Q), 2000)))
+    per_step = min(len(Q), 2000)
     for _ in range(args.warmup):
         o.search(Q[:min(per_step, 256)], TOPK, ef, threads=cores)
     times = []
-    for s in range(args.steps):
-        qb = Q[(s * per_step) % len(Q):][:per_step]
+    for s_ in range(args.steps):
+        qb = Q[(s_ * per_step) % len(Q):][:per_step]
         t0 = time.perf_counter()
         o.search(qb, TOPK, ef, threads=cores)
         times.append((time.perf_counter() - t0, len(qb)))
@@ -268,13 +271,25 @@ def run_reference(args, d: Dist):
     tot_t = sum(t for t, _ in times)
     tot_q = sum(n for _, n in times)
     v = tot_q / tot_t
+    ref_gpu = None
+    if orc.RefGPU.available():
+        clean = Q[flags == 0]
+        r = orc.RefGPU(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], spec.dtype, spec.dim)
+        r.search(clean, TOPK, ef)
+        rts = [r.search(clean, TOPK, ef)[3] for _ in range(args.steps)]
+        r.close()
+        ref_gpu = {"value": len(clean) / float(np.mean(rts)), "unit": "queries/s", "ef_search": ef,
+                   "queries": int(len(clean)),
+                   "what": "the reference's own CUDA kernels (compiled from its sources) on this GPU; "
+                           "GustANNStats.run_time: nav + traversal, host translate included"}
     out = {"impl": "reference", "metric": METRIC, "value": v, "unit": "queries/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot_t / len(times),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
            "data": "synthetic", "config": config_json(args, spec, ef, rec),
            "cpu_baseline": {"value": v, "unit": "queries/s", "cores": cores, "kind": "port",
                             "sample": f"{per_step} queries per step at ef_search={ef}"},
-           "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+           "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "reference_gpu": ref_gpu}
     print(json.dumps(out), flush=True)
 
 
