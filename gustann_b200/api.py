@@ -28,7 +28,8 @@ STATUS_NAMES = ["OK", "EINVAL", "EIO", "ENOMEM", "ECUDA", "ETIMEDOUT", "EUNSUPPO
 EXPORTS = ["gann_open", "gann_open_device", "gann_search", "gann_search_device", "gann_close", "gann_last_error",
            "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample", "gann_set_option",
            "gann_search_noalloc"]
-GANN_OPT_ADC_MODE, GANN_OPT_PIVOT_WARPS = 1, 2
+GANN_OPT_ADC_MODE, GANN_OPT_PIVOT_WARPS, GANN_OPT_NEIGHBOUR_CODES = 1, 2, 3
+LAYOUT_AUTO, LAYOUT_SEPARATE, LAYOUT_NEIGHBOUR_CODES = 0, 1, 2
 ADC_AUTO, ADC_TABLE, ADC_PIVOT = 0, 1, 2
 
 
@@ -42,7 +43,7 @@ class GustANNError(RuntimeError):
 class _Config(C.Structure):
     _fields_ = [("index_file", C.c_char_p), ("pq_file_prefix", C.c_char_p), ("nav_graph_prefix", C.c_char_p),
                 ("dtype", C.c_int32), ("use_gpu_mem", C.c_int32), ("device", C.c_int32),
-                ("reserved", C.c_int32 * 5)]
+                ("layout", C.c_int32), ("reserved", C.c_int32 * 4)]
 
 
 class _Stats(C.Structure):
@@ -125,11 +126,12 @@ class GustANNStats:
 class GustANN:
     """Drop-in for ``gustann::GustANN`` on one B200 (``device``)."""
 
-    def __init__(self, data_type: int = FLOAT, device: int = 0):
+    def __init__(self, data_type: int = FLOAT, device: int = 0, layout: int = 0):
         if data_type not in (UINT8, FLOAT):
             raise GustANNError(GANN_EINVAL, "data type must be UINT8 (0) or FLOAT (1)")
         self.data_type = data_type
         self.device = device
+        self.layout = layout
         self._h = None
         self.dim = 0
 
@@ -139,7 +141,7 @@ class GustANN:
         self.close()
         cfg = _Config(config.index_file.encode(), config.pq_file_prefix.encode(),
                       (config.nav_graph_prefix or "").encode(), self.data_type, int(bool(use_gpu_mem)),
-                      self.device)
+                      self.device, self.layout)
         h = C.c_void_p()
         _check(lib.gann_open(C.byref(cfg), C.byref(h)))
         self._h = h

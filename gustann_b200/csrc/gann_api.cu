@@ -63,6 +63,7 @@ struct gann_handle {
   float* centroid = nullptr;
   int32_t* chunk_off = nullptr;
   float* piv4 = nullptr;
+  uint8_t* ncodes = nullptr;         // neighbour-code copy (layout 0/2)
   uint8_t* nav_vecs = nullptr;
   int32_t* nav_adj = nullptr;
   int32_t* nav_map = nullptr;
@@ -94,7 +95,8 @@ struct gann_handle {
       if (adj) cudaFree(adj);
     }
     for (void* p : {static_cast<void*>(codes), static_cast<void*>(pivots_t), static_cast<void*>(centroid),
-                    static_cast<void*>(chunk_off), static_cast<void*>(piv4), static_cast<void*>(nav_vecs), static_cast<void*>(nav_adj),
+                    static_cast<void*>(chunk_off), static_cast<void*>(piv4), static_cast<void*>(ncodes),
+                    static_cast<void*>(nav_vecs), static_cast<void*>(nav_adj),
                     static_cast<void*>(nav_map), static_cast<void*>(counter), static_cast<void*>(d_q),
                     static_cast<void*>(d_nns), static_cast<void*>(d_dist), static_cast<void*>(d_found),
                     static_cast<void*>(d_hops), static_cast<void*>(d_adc)})
@@ -232,6 +234,25 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
   }
   GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->counter), 4 * sizeof(int32_t)));
   if ((rc = load_records(h, cfg->index_file))) return rc;
+  if (cfg->layout < 0 || cfg->layout > 2) return set_error(GANN_EINVAL, "gann_open: layout must be 0, 1 or 2");
+  if (cfg->layout != 1) {
+    // neighbour codes next to the adjacency: built on the GPU from the records
+    // just loaded (in host-record mode the adjacency is read through UVA)
+    const size_t bytes = static_cast<size_t>(hi.num_points) * ix.adj_stride * ix.code_stride;
+    size_t free_b = 0, total_b = 0;
+    GANN_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    const bool fits = bytes <= total_b / 4 && bytes + (size_t(1) << 30) < free_b;
+    if (cfg->layout == 2 && !fits)
+      return set_error(GANN_ENOMEM, "gann_open: the neighbour-code copy does not fit in device memory");
+    if (fits) {
+      GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->ncodes), bytes));
+      h->device_bytes += static_cast<int64_t>(bytes);
+      GANN_CUDA(gann::launch_gather_neighbour_codes(ix.adj, ix.adj_stride, ix.degree, ix.codes, ix.code_stride,
+                                                    hi.num_points, h->ncodes, h->stream));
+      GANN_CUDA(cudaStreamSynchronize(h->stream));
+      ix.ncodes = h->ncodes;
+    }
+  }
   return GANN_OK;
 }
 
@@ -411,9 +432,15 @@ int gann_set_option(gann_handle* h, int32_t option, int64_t value) {
       h->ix.adc_mode = static_cast<int32_t>(value);
       return GANN_OK;
     case GANN_OPT_PIVOT_WARPS:
-      if (value != 0 && (value < 8 || value > 24))
-        return set_error(GANN_EINVAL, "gann_set_option: pivot warps must be 0 or 8..24");
+      if (value != 0 && (value < 8 || value > 20))
+        return set_error(GANN_EINVAL, "gann_set_option: pivot warps must be 0 or 8..20");
       h->ix.piv_warps = static_cast<int32_t>(value);
+      return GANN_OK;
+    case GANN_OPT_NEIGHBOUR_CODES:
+      if (value != 0 && value != 1) return set_error(GANN_EINVAL, "gann_set_option: neighbour codes must be 0 or 1");
+      if (value == 1 && !h->ncodes)
+        return set_error(GANN_ESTATE, "gann_set_option: the handle was opened without the neighbour-code copy");
+      h->ix.ncodes = value ? h->ncodes : nullptr;
       return GANN_OK;
     default:
       return set_error(GANN_EINVAL, "gann_set_option: unknown option");

@@ -66,6 +66,9 @@ struct DeviceIndex {
   // when every chunk has 3 dims, 4 when all have <= 4, 0 when a chunk is wider
   const float4* piv4 = nullptr;
   int32_t piv_width = 0;
+  // neighbour-code layout: row u = the code rows of adj[u][0..adj_stride),
+  // each code_stride bytes (nullptr when the index keeps codes separate only)
+  const uint8_t* ncodes = nullptr;
   int32_t adc_mode = 0;     // 0 auto, 1 table, 2 pivot
   int32_t piv_warps = 0;    // 0 = as many as fit (<= 24)
 };
@@ -98,6 +101,8 @@ size_t search_smem_bytes(const DeviceIndex& ix, int topk, int ef);
 int make_pivot_table(const std::vector<float>& pivots_t, const std::vector<int32_t>& chunk_off, int dim,
                      std::vector<float>& out);
 int search_max_ef();
+cudaError_t launch_gather_neighbour_codes(const uint32_t* adj, int adj_stride, int degree, const uint8_t* codes,
+                                          int code_stride, int64_t n, uint8_t* out, cudaStream_t st);
 
 // Loader (gann_loader.cpp). Return GANN_* and fill `msg` on error.
 int load_disk_header(const std::string& path, int elem, HostIndex& hi, std::string& msg);

@@ -218,30 +218,32 @@ __device__ __forceinline__ void build_lut(const DeviceIndex& ix, const float* __
   }
 }
 
-// ADC without a per-query table (pivot mode): the table entry of chunk `b` and
+// Sum LUT entries for up to 16 codes packed in `c`, in chunk order.
+__device__ __forceinline__ float adc16(float s, const uint4 c, const float* __restrict__ lut, int n) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int b = 0; b < 16; ++b) {
+    if (b < n) s = __fadd_rn(s, lut[b * kPivots + ((w[b >> 2] >> (8 * (b & 3))) & 0xffu)]);
+  }
+  return s;
+}
+
+// The same sums without a per-query table: the table entry of chunk `b` and
 // code `j` is recomputed from the CTA-resident pivot row piv[b][j] (zero-padded
 // to 4 dims) and the query residual qcp[b] -- d = qc_i - p_ji, e = fma(d, d, e)
 // from 0 over the chunk's dims in order, then s += e -- which are the fp32
 // operations that produce and consume the reference's table entry, so the sum
 // is bit-identical. CW = dims per chunk (4 also serves mixed widths <= 4: the
 // zero padding contributes fma(0, 0, e) = e).
-
-// Four chunks at a time (one 32-bit word of codes), for the early exit below.
-__device__ __forceinline__ float adc4(float s, uint32_t w, const float* __restrict__ lut, int n) {
-#pragma unroll
-  for (int b = 0; b < 4; ++b)
-    if (b < n) s = __fadd_rn(s, lut[b * kPivots + ((w >> (8 * b)) & 0xffu)]);
-  return s;
-}
-
 template <int CW>
-__device__ __forceinline__ float adc4_piv(float s, uint32_t w, const float4* __restrict__ piv,
-                                          const float4* __restrict__ qcp, int n) {
+__device__ __forceinline__ float adc16_piv(float s, const uint4 c, const float4* __restrict__ piv,
+                                           const float4* __restrict__ qcp, int n) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-  for (int b = 0; b < 4; ++b) {
+  for (int b = 0; b < 16; ++b) {
     if (b < n) {
       const float4 q = qcp[b];
-      const float4 p = piv[b * kPivots + ((w >> (8 * b)) & 0xffu)];
+      const float4 p = piv[b * kPivots + ((w[b >> 2] >> (8 * (b & 3))) & 0xffu)];
       float d = __fsub_rn(q.x, p.x);
       float e = __fmul_rn(d, d);
       d = __fsub_rn(q.y, p.y);
@@ -256,12 +258,6 @@ __device__ __forceinline__ float adc4_piv(float s, uint32_t w, const float4* __r
     }
   }
   return s;
-}
-
-// Distance held in a pool key (inverse of ord_f32).
-__device__ __forceinline__ float key_dist(uint64_t key) {
-  const uint32_t o = static_cast<uint32_t>(key >> 32);
-  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
 }
 
 struct WarpSmem {
@@ -325,21 +321,49 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
 }
 
 // Neighbour ids (padding = kPadId) and the vector elements lane l owns
-// (dims l, l+32, ...) of one record.
+// (dims l, l+32, ...) of one record; with the neighbour-code layout also the
+// first two 16-byte code words of the lane's neighbours, whose address depends
+// only on the node.
 template <typename T, int NPL, int VP>
 __device__ __forceinline__ void load_node(const DeviceIndex& ix, uint32_t u, int lane, uint32_t (&nb)[NPL],
-                                          float (&xv)[VP]) {
+                                          float (&xv)[VP], uint4 (&c0)[NPL], uint4 (&c1)[NPL]) {
   const uint32_t* arow = ix.adj + static_cast<size_t>(u) * ix.adj_stride;
 #pragma unroll
   for (int k = 0; k < NPL; ++k) {
     const int e = lane + kWarp * k;
     nb[k] = e < ix.degree ? __ldg(arow + e) : kPadId;
   }
+  if (ix.ncodes != nullptr) {
+    const uint8_t* crow = ix.ncodes + static_cast<size_t>(u) * ix.adj_stride * ix.code_stride;
+    const bool two = ix.code_stride > 16;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      const int e = lane + kWarp * k;
+      const uint4* p = reinterpret_cast<const uint4*>(crow + static_cast<size_t>(e) * ix.code_stride);
+      c0[k] = e < ix.degree ? __ldg(p) : make_uint4(0, 0, 0, 0);
+      c1[k] = (two && e < ix.degree) ? __ldg(p + 1) : make_uint4(0, 0, 0, 0);
+    }
+  }
   const T* xr = reinterpret_cast<const T*>(ix.vecs) + static_cast<size_t>(u) * (ix.vec_stride / sizeof(T));
 #pragma unroll
   for (int v = 0; v < VP; ++v) {
     const int i = lane + kWarp * v;
     xv[v] = i < ix.dim ? static_cast<float>(__ldg(xr + i)) : 0.f;
+  }
+}
+
+// Code gather for the neighbour-code layout: out row u, slot k = codes of
+// adj[u][k] (zeros for empty slots). One thread per 16-byte word.
+__global__ void gather_neighbour_codes(const uint32_t* __restrict__ adj, int adj_stride, int degree,
+                                       const uint4* __restrict__ codes, int words, int64_t n, uint4* __restrict__ out) {
+  const int64_t total = n * adj_stride * words;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t slot = i / words;
+    const int w = static_cast<int>(i % words);
+    const int k = static_cast<int>(slot % adj_stride);
+    const uint32_t v = k < degree ? __ldg(adj + slot) : kPadId;
+    out[i] = v != kPadId ? __ldg(codes + static_cast<int64_t>(v) * words + w) : make_uint4(0, 0, 0, 0);
   }
 }
 
@@ -378,7 +402,8 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
   }
   uint32_t nb[NPL];
   float xv[VP];
-  load_node<T, NPL, VP>(ix, u, lane, nb, xv);
+  uint4 c0[NPL], c1[NPL];
+  load_node<T, NPL, VP>(ix, u, lane, nb, xv, c0, c1);
   __syncwarp();
 
   for (;;) {
@@ -389,13 +414,18 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     ++hops;
     bool ok[NPL];
     const uint4* crow[NPL];
-    uint4 cur[NPL];
+    const bool inl = ix.ncodes != nullptr;
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
       adc += __popc(__ballot_sync(kFull, nb[k] != kPadId));
       ok[k] = nb[k] != kPadId && s.filt[fslot(nb[k])] != nb[k];
-      crow[k] = reinterpret_cast<const uint4*>(ix.codes + static_cast<size_t>(ok[k] ? nb[k] : 0) * ix.code_stride);
-      cur[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
+      crow[k] = reinterpret_cast<const uint4*>(
+          inl ? ix.ncodes + (static_cast<size_t>(u) * ix.adj_stride + lane + kWarp * k) * ix.code_stride
+              : ix.codes + static_cast<size_t>(ok[k] ? nb[k] : 0) * ix.code_stride);
+      if (!inl) {
+        c0[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
+        c1[k] = (ok[k] && mw > 1) ? __ldg(crow[k] + 1) : make_uint4(0, 0, 0, 0);
+      }
     }
 
     // first unvisited pool entry; every entry before `pfirst` is visited
@@ -412,61 +442,30 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     const uint64_t pstar = ppos >= 0 ? s.pool[ppos] : ~0ull;
 
     // ADC of every neighbour not known to be in the pool, one lane per
-    // neighbour, chunks in order. With a full pool a neighbour whose partial
-    // sum already exceeds the last entry's distance is settled: table entries
-    // are >= 0 and round-to-nearest sums of them never decrease, so its final
-    // key lies beyond the last entry and the merge would drop it -- its
-    // remaining chunks are skipped, and the warp leaves once no lane is live.
+    // neighbour, chunks in order
     float dsum[NPL];
-    bool live[NPL];
 #pragma unroll
-    for (int k = 0; k < NPL; ++k) {
-      dsum[k] = 0.f;
-      live[k] = ok[k];
-    }
-    const bool full = psize == L;
-    const float lastd = full ? key_dist(s.pool[L - 1]) : INFINITY;
+    for (int k = 0; k < NPL; ++k) dsum[k] = 0.f;
     for (int w = 0; w < mw; ++w) {
-      uint4 nxt[NPL];
-      const bool more = w + 1 < mw;
+      uint4 cur[NPL];
 #pragma unroll
-      for (int k = 0; k < NPL; ++k) nxt[k] = (more && live[k]) ? __ldg(crow[k] + w + 1) : make_uint4(0, 0, 0, 0);
+      for (int k = 0; k < NPL; ++k)
+        cur[k] = w == 0 ? c0[k] : w == 1 ? c1[k] : (ok[k] ? __ldg(crow[k] + w) : make_uint4(0, 0, 0, 0));
       const int n = min(16, M - 16 * w);
-      bool any = true;
+      if (PIV == 0) {
+        const float* lw = s.lut + 16 * w * kPivots;
 #pragma unroll
-      for (int sub = 0; sub < 4; ++sub) {
-        const int nc = n - 4 * sub;
-        if (nc <= 0) break;
+        for (int k = 0; k < NPL; ++k)
+          if (ok[k]) dsum[k] = adc16(dsum[k], cur[k], lw, n);
+      } else {
+        const float4* pw = piv + 16 * w * kPivots;
+        const float4* qw = s.qcp + 16 * w;
 #pragma unroll
-        for (int k = 0; k < NPL; ++k) {
-          if (live[k]) {
-            const uint32_t wd = sub == 0 ? cur[k].x : sub == 1 ? cur[k].y : sub == 2 ? cur[k].z : cur[k].w;
-            const int c0 = 16 * w + 4 * sub;
-            if (PIV == 0)
-              dsum[k] = adc4(dsum[k], wd, s.lut + c0 * kPivots, nc);
-            else if (PIV == 3)
-              dsum[k] = adc4_piv<3>(dsum[k], wd, piv + c0 * kPivots, s.qcp + c0, nc);
-            else
-              dsum[k] = adc4_piv<4>(dsum[k], wd, piv + c0 * kPivots, s.qcp + c0, nc);
-          }
-        }
-        if (full) {
-          bool l = false;
-#pragma unroll
-          for (int k = 0; k < NPL; ++k) {
-            live[k] = live[k] && !(dsum[k] > lastd);
-            l = l || live[k];
-          }
-          any = __any_sync(kFull, l);
-          if (!any) break;
-        }
+        for (int k = 0; k < NPL; ++k)
+          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3>(dsum[k], cur[k], pw, qw, n)
+                                        : adc16_piv<4>(dsum[k], cur[k], pw, qw, n);
       }
-#pragma unroll
-      for (int k = 0; k < NPL; ++k) cur[k] = nxt[k];
-      if (!any) break;
     }
-#pragma unroll
-    for (int k = 0; k < NPL; ++k) ok[k] = ok[k] && live[k];
 
     // candidates that can enter the pool: not beyond its last entry when full,
     // not already in it; rank = insertion point (lower bound on (dist, id))
@@ -503,8 +502,9 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     const bool more = nxt != ~0ull;
     uint32_t nb2[NPL];
     float xv2[VP];
+    uint4 c02[NPL], c12[NPL];
     if (more) {
-      load_node<T, NPL, VP>(ix, static_cast<uint32_t>(nxt) >> 1, lane, nb2, xv2);
+      load_node<T, NPL, VP>(ix, static_cast<uint32_t>(nxt) >> 1, lane, nb2, xv2, c02, c12);
     } else {
 #pragma unroll
       for (int k = 0; k < NPL; ++k) nb2[k] = kPadId;
@@ -653,7 +653,11 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     if (!more) break;
     u = static_cast<uint32_t>(nxt) >> 1;
 #pragma unroll
-    for (int k = 0; k < NPL; ++k) nb[k] = nb2[k];
+    for (int k = 0; k < NPL; ++k) {
+      nb[k] = nb2[k];
+      c0[k] = c02[k];
+      c1[k] = c12[k];
+    }
 #pragma unroll
     for (int v = 0; v < VP; ++v) xv[v] = xv2[v];
   }
@@ -732,7 +736,7 @@ __global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, con
 // Pivot mode: one persistent CTA per SM holds the 256 x D pivot table once
 // (M x 4 KB) and runs up to kPivWarps queries at a time, one per warp, each
 // with a few KB of private state instead of a 4*M KB table.
-constexpr int kPivWarps = 24;
+constexpr int kPivWarps = 20;
 template <typename T, int NPL, int VP, int CW>
 __global__ void __launch_bounds__(kWarp * kPivWarps, 1) search_kernel_piv(const DeviceIndex ix, const SearchArgs a,
                                                                           size_t per_warp, int pl) {
@@ -840,6 +844,13 @@ cudaError_t launch_typed(const DeviceIndex& ix, const SearchArgs& a, int sm_coun
 }
 
 }  // namespace
+
+cudaError_t launch_gather_neighbour_codes(const uint32_t* adj, int adj_stride, int degree, const uint8_t* codes,
+                                          int code_stride, int64_t n, uint8_t* out, cudaStream_t st) {
+  gather_neighbour_codes<<<148 * 8, 256, 0, st>>>(adj, adj_stride, degree, reinterpret_cast<const uint4*>(codes),
+                                                  code_stride / 16, n, reinterpret_cast<uint4*>(out));
+  return cudaGetLastError();
+}
 
 int search_max_ef() { return 32 * kWarp; }
 

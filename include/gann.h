@@ -51,6 +51,12 @@ typedef enum { GANN_UINT8 = 0, GANN_FLOAT = 1 } gann_dtype;
  *   use_gpu_mem       1: records in HBM ("-G"); 0: records in pinned host
  *                     memory, read by the GPU over the host link
  *   device            CUDA device ordinal
+ *   layout            0 auto, 1 PQ codes only in their own array, 2 also a
+ *                     copy of every node's neighbours' codes next to its
+ *                     adjacency (N x R x M bytes of HBM; a hop then reads one
+ *                     contiguous record). Auto builds the copy when it takes at
+ *                     most a quarter of the device's memory. No counterpart in
+ *                     the reference, which keeps one code array.
  */
 typedef struct {
   const char* index_file;
@@ -59,7 +65,8 @@ typedef struct {
   int32_t dtype;
   int32_t use_gpu_mem;
   int32_t device;
-  int32_t reserved[5];
+  int32_t layout;
+  int32_t reserved[4];
 } gann_config;
 
 /* Replaces gustann::GustANNStats (src/ssd_search.hpp:25-27) and adds the
@@ -188,8 +195,10 @@ int gann_close(gann_handle* h);
  *     PQ pivot table resident once per SM with table entries recomputed per
  *     lookup (bit-identical sums; needs <= 4 dims per chunk and D <= 128).
  *     Auto picks 2 when it fits.
- *   GANN_OPT_PIVOT_WARPS: queries in flight per SM in mode 2 (8..24, 0 auto). */
-enum { GANN_OPT_ADC_MODE = 1, GANN_OPT_PIVOT_WARPS = 2 };
+ *   GANN_OPT_PIVOT_WARPS: queries in flight per SM in mode 2 (8..20, 0 auto).
+ *   GANN_OPT_NEIGHBOUR_CODES: 1 read neighbour codes from the per-node copy
+ *     when the handle has one (layout 0/2), 0 from the shared code array. */
+enum { GANN_OPT_ADC_MODE = 1, GANN_OPT_PIVOT_WARPS = 2, GANN_OPT_NEIGHBOUR_CODES = 3 };
 int gann_set_option(gann_handle* h, int32_t option, int64_t value);
 
 /* Message of the last failed call on this thread ("" if none). */

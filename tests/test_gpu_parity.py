@@ -30,17 +30,20 @@ def _oracle(info, nav=True):
     return Oracle(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"] if nav else "", info["dtype"])
 
 
-@pytest.fixture(scope="module", params=["auto", "table"])
+@pytest.fixture(scope="module", params=["auto", "table", "separate-codes"])
 def handles(index_root, request):
-    """Every index opened twice over the module: ADC mode auto (pivot-resident
-    wherever it fits) and forced per-query table mode."""
-    from gustann_b200.api import ADC_TABLE, GANN_OPT_ADC_MODE
+    """Every index opened over the module in three configurations: ADC mode
+    auto (pivot-resident wherever it fits) with the neighbour-code copy, forced
+    per-query table mode, and codes read from the shared code array."""
+    from gustann_b200.api import ADC_TABLE, GANN_OPT_ADC_MODE, GANN_OPT_NEIGHBOUR_CODES
     out = {}
     for name in INDEXES:
         info = get_index(index_root, name)
         g = _open(info)
         if request.param == "table":
             g.set_option(GANN_OPT_ADC_MODE, ADC_TABLE)
+        if request.param == "separate-codes":
+            g.set_option(GANN_OPT_NEIGHBOUR_CODES, 0)
         out[name] = (info, g, _oracle(info))
     yield out
     for _, g, o in out.values():
@@ -213,7 +216,7 @@ def test_pivot_mode_option(index_root):
     g.set_option(GANN_OPT_ADC_MODE, ADC_TABLE)
     ref = g.query(q, 10, 48)
     g.set_option(GANN_OPT_ADC_MODE, ADC_PIVOT)
-    for w in (8, 13, 24, 0):
+    for w in (8, 13, 20, 0):
         g.set_option(GANN_OPT_PIVOT_WARPS, w)
         out = g.query(q, 10, 48)
         for u, v in zip(ref, out):
