@@ -20,6 +20,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import subprocess
 import sys
 import threading
@@ -161,12 +162,23 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def traffic_per_launch(cfg_key: str):
-    """DRAM bytes per launch from the committed ncu summary, if one exists."""
-    p = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(p):
-        with open(p) as f:
-            return json.load(f).get(cfg_key)
+def traffic_per_launch(cfg_key: str, n: int, ef: int):
+    """DRAM bytes (read + write) per launch of the search kernel, from a
+    committed ncu summary under profiles/ that names this workload:
+    a line `traffic_bytes_per_launch <config> n=<points> ef=<ef>: <bytes>`.
+    None when no capture of this exact workload was committed."""
+    d = os.path.join(ROOT, "profiles")
+    pat = re.compile(r"^traffic_bytes_per_launch (\S+) n=(\d+) ef=(\d+): (\d+)\s*$")
+    if not os.path.isdir(d):
+        return None
+    for name in sorted(os.listdir(d)):
+        if not name.endswith(".md"):
+            continue
+        with open(os.path.join(d, name)) as f:
+            for line in f:
+                m = pat.match(line.strip())
+                if m and m.group(1) == cfg_key and int(m.group(2)) == n and int(m.group(3)) == ef:
+                    return int(m.group(4))
     return None
 
 
@@ -382,7 +394,7 @@ def run_ours(args, d: Dist):
 
     peak, peak_kind = measured_peak()
     achieved = st.bytes_touched / (np.mean(step_ms) * 1e-3) / 1e9
-    traffic = traffic_per_launch(args.config)
+    traffic = traffic_per_launch(args.config, spec.n, ef)
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
             "algorithmic_bytes_per_launch": int(st.bytes_touched),
