@@ -73,7 +73,7 @@ class Dist:
         if self.world > 1:
             import datetime
             torch.cuda.set_device(self.local)
-            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(minutes=30),
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(minutes=10),
                                                  device_id=torch.device("cuda", self.local))
             self.pg = True
         elif torch.cuda.is_available():

@@ -228,22 +228,45 @@ __device__ __forceinline__ float adc16(float s, const uint4 c, const float* __re
   return s;
 }
 
+// CTA-resident PQ pivot table, row r = chunk * 256 + code. With 3 dims per
+// chunk the rows are split into an (x, y) float2 plane and a z float plane:
+// 12 B per pivot, gathered with one 8-byte and one 4-byte shared load, which
+// costs fewer bank-conflict wavefronts for 32 random rows than one padded
+// 16-byte row (about 9.0 against 10.2). Chunks of up to 4 dims keep float4
+// rows, zero-padded.
+struct PivTab {
+  const float2* xy;
+  const float* z;
+  const float4* xyzw;
+};
+
+__host__ __device__ inline size_t piv_tab_bytes(int cw, int chunks) {
+  return static_cast<size_t>(cw == 3 ? 12 : 16) * chunks * kPivots;
+}
+
 // The same sums without a per-query table: the table entry of chunk `b` and
-// code `j` is recomputed from the CTA-resident pivot row piv[b][j] (zero-padded
-// to 4 dims) and the query residual qcp[b] -- d = qc_i - p_ji, e = fma(d, d, e)
-// from 0 over the chunk's dims in order, then s += e -- which are the fp32
-// operations that produce and consume the reference's table entry, so the sum
-// is bit-identical. CW = dims per chunk (4 also serves mixed widths <= 4: the
-// zero padding contributes fma(0, 0, e) = e).
+// code `j` is recomputed from the pivot row of (b, j) and the query residual
+// qcp[b] -- d = qc_i - p_ji, e = fma(d, d, e) from 0 over the chunk's dims in
+// order, then s += e -- which are the fp32 operations that produce and consume
+// the reference's table entry, so the sum is bit-identical. CW = dims per
+// chunk (4 also serves mixed widths <= 4: the zero padding contributes
+// fma(0, 0, e) = e). `row0` is the first row of this 16-chunk group.
 template <int CW>
-__device__ __forceinline__ float adc16_piv(float s, const uint4 c, const float4* __restrict__ piv,
+__device__ __forceinline__ float adc16_piv(float s, const uint4 c, const PivTab& t, int row0,
                                            const float4* __restrict__ qcp, int n) {
   const uint32_t w[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
   for (int b = 0; b < 16; ++b) {
     if (b < n) {
       const float4 q = qcp[b];
-      const float4 p = piv[b * kPivots + ((w[b >> 2] >> (8 * (b & 3))) & 0xffu)];
+      const int r = row0 + b * kPivots + static_cast<int>((w[b >> 2] >> (8 * (b & 3))) & 0xffu);
+      float4 p;
+      if (CW == 3) {
+        const float2 xy = t.xy[r];
+        p = make_float4(xy.x, xy.y, t.z[r], 0.f);
+      } else {
+        p = t.xyzw[r];
+      }
       float d = __fsub_rn(q.x, p.x);
       float e = __fmul_rn(d, d);
       d = __fsub_rn(q.y, p.y);
@@ -300,7 +323,7 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
   unsigned char* pool = take(sizeof(uint64_t) * pl * kWarp);
   unsigned char* cand = take(sizeof(uint64_t) * npl * kWarp);
   unsigned char* candr = take(sizeof(int) * npl * kWarp);
-  unsigned char* hist = take(sizeof(int) * ((pl > npl ? pl : npl) * kWarp + kWarp));
+  unsigned char* hist = take(sizeof(int) * npl * kWarp);
   unsigned char* filt = take(sizeof(uint32_t) << filt_bits(pl));
   unsigned char* topd = take(sizeof(float) * topk);
   unsigned char* topi = take(sizeof(int) * topk);
@@ -321,12 +344,13 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
 }
 
 // Neighbour ids (padding = kPadId) and the vector elements lane l owns
-// (dims l, l+32, ...) of one record; with the neighbour-code layout also the
-// first two 16-byte code words of the lane's neighbours, whose address depends
-// only on the node.
+// (dims l, l+32, ...) of one record. With the neighbour-code layout the node's
+// block of neighbour code rows, whose address depends only on the node, is
+// prefetched into L2 (no registers held while the merge runs; the hop that
+// expands the node loads the rows it needs from L2).
 template <typename T, int NPL, int VP>
 __device__ __forceinline__ void load_node(const DeviceIndex& ix, uint32_t u, int lane, uint32_t (&nb)[NPL],
-                                          float (&xv)[VP], uint4 (&c0)[NPL], uint4 (&c1)[NPL]) {
+                                          float (&xv)[VP]) {
   const uint32_t* arow = ix.adj + static_cast<size_t>(u) * ix.adj_stride;
 #pragma unroll
   for (int k = 0; k < NPL; ++k) {
@@ -335,13 +359,10 @@ __device__ __forceinline__ void load_node(const DeviceIndex& ix, uint32_t u, int
   }
   if (ix.ncodes != nullptr) {
     const uint8_t* crow = ix.ncodes + static_cast<size_t>(u) * ix.adj_stride * ix.code_stride;
-    const bool two = ix.code_stride > 16;
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
       const int e = lane + kWarp * k;
-      const uint4* p = reinterpret_cast<const uint4*>(crow + static_cast<size_t>(e) * ix.code_stride);
-      c0[k] = e < ix.degree ? __ldg(p) : make_uint4(0, 0, 0, 0);
-      c1[k] = (two && e < ix.degree) ? __ldg(p + 1) : make_uint4(0, 0, 0, 0);
+      if (e < ix.degree) asm volatile("prefetch.global.L2 [%0];" ::"l"(crow + static_cast<size_t>(e) * ix.code_stride));
     }
   }
   const T* xr = reinterpret_cast<const T*>(ix.vecs) + static_cast<size_t>(u) * (ix.vec_stride / sizeof(T));
@@ -372,8 +393,9 @@ __global__ void gather_neighbour_codes(const uint32_t* __restrict__ adj, int adj
 // The node expanded next is min(first unvisited pool entry, best candidate
 // that enters the pool) -- exactly the first unvisited entry of the merged
 // pool -- so it is known right after the ADC step. Its record is requested
-// then, and the merge and the top-k insert of the current node run while that
-// load is in flight.
+// then (adjacency and vector into registers, neighbour code rows into L2), and
+// the merge and the top-k insert of the current node run while those loads are
+// in flight.
 //
 // A neighbour that is already in the pool would be dropped as a duplicate of
 // the pool copy (same id, hence same PQ distance), so its code row and ADC are
@@ -382,7 +404,7 @@ __global__ void gather_neighbour_codes(const uint32_t* __restrict__ adj, int adj
 // (written when it enters, cleared when it is pushed out past `ef`).
 template <typename T, int NPL, int VP, int PIV>
 __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid, uint32_t entry,
-                         const WarpSmem& s, const float4* __restrict__ piv, int lane, int pl) {
+                         const WarpSmem& s, const PivTab& piv, int lane, int pl) {
   const int dim = ix.dim, M = ix.chunks, L = a.ef, topk = a.topk;
   const int mw = ix.code_stride >> 4;
   const int fbits = filt_bits(pl);
@@ -402,8 +424,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
   }
   uint32_t nb[NPL];
   float xv[VP];
-  uint4 c0[NPL], c1[NPL];
-  load_node<T, NPL, VP>(ix, u, lane, nb, xv, c0, c1);
+  load_node<T, NPL, VP>(ix, u, lane, nb, xv);
   __syncwarp();
 
   for (;;) {
@@ -412,8 +433,11 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       break;
     }
     ++hops;
+    // code rows of the neighbours to evaluate: slot k of u's neighbour-code
+    // block (prefetched into L2 when u was chosen), else row nb[k] of `codes`
     bool ok[NPL];
     const uint4* crow[NPL];
+    uint4 c0[NPL], c1[NPL];
     const bool inl = ix.ncodes != nullptr;
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
@@ -422,10 +446,8 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       crow[k] = reinterpret_cast<const uint4*>(
           inl ? ix.ncodes + (static_cast<size_t>(u) * ix.adj_stride + lane + kWarp * k) * ix.code_stride
               : ix.codes + static_cast<size_t>(ok[k] ? nb[k] : 0) * ix.code_stride);
-      if (!inl) {
-        c0[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
-        c1[k] = (ok[k] && mw > 1) ? __ldg(crow[k] + 1) : make_uint4(0, 0, 0, 0);
-      }
+      c0[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
+      c1[k] = (ok[k] && mw > 1) ? __ldg(crow[k] + 1) : make_uint4(0, 0, 0, 0);
     }
 
     // first unvisited pool entry; every entry before `pfirst` is visited
@@ -458,17 +480,18 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
         for (int k = 0; k < NPL; ++k)
           if (ok[k]) dsum[k] = adc16(dsum[k], cur[k], lw, n);
       } else {
-        const float4* pw = piv + 16 * w * kPivots;
         const float4* qw = s.qcp + 16 * w;
 #pragma unroll
         for (int k = 0; k < NPL; ++k)
-          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3>(dsum[k], cur[k], pw, qw, n)
-                                        : adc16_piv<4>(dsum[k], cur[k], pw, qw, n);
+          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, n)
+                                        : adc16_piv<4>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, n);
       }
     }
 
     // candidates that can enter the pool: not beyond its last entry when full,
-    // not already in it; rank = insertion point (lower bound on (dist, id))
+    // not already in it; rank = insertion point (lower bound on (dist, id)),
+    // found by power-of-two steps with a warp-uniform trip count and the NPL
+    // searches of a lane interleaved (independent shared loads in flight)
     uint64_t key[NPL];
     int rk[NPL];
     const uint64_t last = psize == L ? (s.pool[L - 1] >> 1) : ~0ull;
@@ -477,20 +500,20 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     for (int k = 0; k < NPL; ++k) {
       key[k] = make_key(dsum[k], nb[k]);
       rk[k] = 0;
-      if (ok[k]) {
-        const uint64_t kk = key[k] >> 1;
-        if (kk >= last) {
-          ok[k] = false;
-        } else {
-          int lo = 0, hi = psize;
-          while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if ((s.pool[mid] >> 1) < kk) lo = mid + 1; else hi = mid;
-          }
-          rk[k] = lo;
-          if (lo < psize && (s.pool[lo] >> 1) == kk) ok[k] = false;
+      if (ok[k] && (key[k] >> 1) >= last) ok[k] = false;
+    }
+    if (psize > 0) {
+      for (int step = 1 << (31 - __clz(psize)); step > 0; step >>= 1) {
+#pragma unroll
+        for (int k = 0; k < NPL; ++k) {
+          const int t = rk[k] + step;
+          if (ok[k] && t <= psize && (s.pool[t - 1] >> 1) < (key[k] >> 1)) rk[k] = t;
         }
       }
+    }
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      if (ok[k] && rk[k] < psize && (s.pool[rk[k]] >> 1) == (key[k] >> 1)) ok[k] = false;
       if (ok[k] && key[k] < mk) mk = key[k];
     }
 #pragma unroll
@@ -502,9 +525,8 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     const bool more = nxt != ~0ull;
     uint32_t nb2[NPL];
     float xv2[VP];
-    uint4 c02[NPL], c12[NPL];
     if (more) {
-      load_node<T, NPL, VP>(ix, static_cast<uint32_t>(nxt) >> 1, lane, nb2, xv2, c02, c12);
+      load_node<T, NPL, VP>(ix, static_cast<uint32_t>(nxt) >> 1, lane, nb2, xv2);
     } else {
 #pragma unroll
       for (int k = 0; k < NPL; ++k) nb2[k] = kPadId;
@@ -602,23 +624,33 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
         if (lane + kWarp * k < S) s.hist[cpos[k] - cr[k]] = cr[k];
       __syncwarp();
       // moves, four chunks at a time from the last one down (an entry only moves
-      // right); entries pushed past `ef` leave the pool and the membership table
+      // right); entries pushed past `ef` leave the pool and the membership table.
+      // The shift of entry i is an upper bound in hist, found by power-of-two
+      // steps with the four chunks' searches interleaved.
       const int j0 = rmin >> 5;
+      const int sstep = 1 << (31 - __clz(S));
       for (int jg = (psize - 1) >> 5; jg >= j0; jg -= 4) {
         uint64_t v[4];
-        int dst[4];
+        int dst[4], sh[4];
+        bool act[4];
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           const int i = lane + kWarp * (jg - g);
-          dst[g] = INT_MAX;
-          v[g] = 0;
-          if (jg - g >= j0 && i < psize) {
-            v[g] = s.pool[i];
-            int t = 0;
-            while (t < S && s.hist[t] <= i) ++t;
-            dst[g] = i + t;
-            if (v[g] == nxt) v[g] &= ~1ull;
+          act[g] = jg - g >= j0 && i < psize;
+          v[g] = act[g] ? s.pool[i] : 0;
+          sh[g] = 0;
+        }
+        for (int step = sstep; step > 0; step >>= 1) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int t = sh[g] + step;
+            if (act[g] && t <= S && s.hist[t - 1] <= lane + kWarp * (jg - g)) sh[g] = t;
           }
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          dst[g] = act[g] ? lane + kWarp * (jg - g) + sh[g] : INT_MAX;
+          if (v[g] == nxt) v[g] &= ~1ull;
         }
         __syncwarp();
 #pragma unroll
@@ -653,11 +685,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     if (!more) break;
     u = static_cast<uint32_t>(nxt) >> 1;
 #pragma unroll
-    for (int k = 0; k < NPL; ++k) {
-      nb[k] = nb2[k];
-      c0[k] = c02[k];
-      c1[k] = c12[k];
-    }
+    for (int k = 0; k < NPL; ++k) nb[k] = nb2[k];
 #pragma unroll
     for (int v = 0; v < VP; ++v) xv[v] = xv2[v];
   }
@@ -680,7 +708,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
 // One query per warp, from query setup to the written top-k.
 template <typename T, int NPL, int VP, int PIV>
 __device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchArgs& a, const WarpSmem& s,
-                                            const float4* __restrict__ piv, int lane, int pl) {
+                                            const PivTab& piv, int lane, int pl) {
   const int dim = ix.dim;
   for (;;) {
     int qid = 0;
@@ -730,24 +758,39 @@ __global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, con
   extern __shared__ __align__(16) unsigned char smem[];
   WarpSmem s;
   carve(smem, ix.chunks, ix.dim, NPL, pl, a.topk, &s, false);
-  run_queries<T, NPL, VP, 0>(ix, a, s, nullptr, threadIdx.x, pl);
+  run_queries<T, NPL, VP, 0>(ix, a, s, PivTab{nullptr, nullptr, nullptr}, threadIdx.x, pl);
 }
 
 // Pivot mode: one persistent CTA per SM holds the 256 x D pivot table once
-// (M x 4 KB) and runs up to kPivWarps queries at a time, one per warp, each
-// with a few KB of private state instead of a 4*M KB table.
+// (M x 3 KB for 3-dim chunks, M x 4 KB otherwise) and runs up to kPivWarps
+// queries at a time, one per warp, each with a few KB of private state instead
+// of a 4*M KB table.
 constexpr int kPivWarps = 20;
 template <typename T, int NPL, int VP, int CW>
 __global__ void __launch_bounds__(kWarp * kPivWarps, 1) search_kernel_piv(const DeviceIndex ix, const SearchArgs a,
                                                                           size_t per_warp, int pl) {
   extern __shared__ __align__(16) unsigned char smem[];
-  float4* piv = reinterpret_cast<float4*>(smem);
   const int ntab = ix.chunks * kPivots;
-  for (int i = threadIdx.x; i < ntab; i += blockDim.x) piv[i] = __ldg(ix.piv4 + i);
+  PivTab piv{nullptr, nullptr, nullptr};
+  if (CW == 3) {
+    float2* xy = reinterpret_cast<float2*>(smem);
+    float* z = reinterpret_cast<float*>(xy + ntab);
+    for (int i = threadIdx.x; i < ntab; i += blockDim.x) {
+      const float4 p = __ldg(ix.piv4 + i);
+      xy[i] = make_float2(p.x, p.y);
+      z[i] = p.z;
+    }
+    piv.xy = xy;
+    piv.z = z;
+  } else {
+    float4* t = reinterpret_cast<float4*>(smem);
+    for (int i = threadIdx.x; i < ntab; i += blockDim.x) t[i] = __ldg(ix.piv4 + i);
+    piv.xyzw = t;
+  }
   __syncthreads();
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   WarpSmem s;
-  carve(smem + sizeof(float4) * ntab + per_warp * warp, ix.chunks, ix.dim, NPL, pl, a.topk, &s, true);
+  carve(smem + piv_tab_bytes(CW, ix.chunks) + per_warp * warp, ix.chunks, ix.dim, NPL, pl, a.topk, &s, true);
   run_queries<T, NPL, VP, CW>(ix, a, s, piv, lane, pl);
 }
 
@@ -800,7 +843,7 @@ cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_co
   if constexpr (VP == 4) if (ix.piv_width > 0 && ix.adc_mode != 1) {
     // pivot mode when the table plus at least 8 warps' state fit (dims <= 128;
     // wider vectors have too many chunks for a shared-memory pivot table)
-    const size_t tab = sizeof(float4) * ix.chunks * kPivots;
+    const size_t tab = piv_tab_bytes(ix.piv_width, ix.chunks);
     const size_t per_warp = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, true);
     int warps = tab < static_cast<size_t>(optin)
                     ? static_cast<int>(std::min<size_t>(kPivWarps, (optin - tab) / per_warp)) : 0;
