@@ -103,42 +103,59 @@ class Dist:
 
 
 class Clocks:
-    """nvidia-smi sampling while the timed region runs."""
+    """nvidia-smi sampling (every 20 ms) around the timed region; stop() keeps
+    the samples that arrived inside it (the nearest ones on either side when
+    the region is shorter than one period)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, dev: int):
+        # nvidia-smi numbers GPUs physically; address this process's GPU by UUID
+        try:
+            self.id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+        except Exception:
+            self.id = str(dev)
         self.p = None
         self.lines = []
 
-    def start(self):
+    def start(self, wait_s: float = 5.0):
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.id}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "20"],
                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:
             self.p = None
+            return
+        t0 = time.perf_counter()
+        while not self.lines and time.perf_counter() - t0 < wait_s and self.p.poll() is None:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.p.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
 
-    def stop(self) -> dict:
+    def stop(self, t_begin: float, t_end: float) -> dict:
         if not self.p:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.05)
         self.p.terminate()
         try:
             self.p.wait(timeout=5)
         except Exception:
             self.p.kill()
+        inside = [ln for t, ln in self.lines if t_begin <= t <= t_end + 0.025]
+        where = "inside the timed region"
+        if not inside:
+            before = [ln for t, ln in self.lines if t < t_begin][-1:]
+            after = [ln for t, ln in self.lines if t > t_end][:1]
+            inside, where = before + after, "nearest samples around a region shorter than the 20 ms period"
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in inside:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -151,7 +168,7 @@ class Clocks:
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": where}
 
 
 def measured_peak():
@@ -361,14 +378,16 @@ def run_ours(args, d: Dist):
     d.barrier()
     torch.cuda.synchronize(dev)
     torch.cuda.cudart().cudaProfilerStart()      # a profiler started with --profile-from-start off sees only this
+    t_begin = time.perf_counter()
     for a, b in evs:
         a.record(stream)
         launch()
         b.record(stream)
     torch.cuda.synchronize(dev)
+    t_end = time.perf_counter()
     torch.cuda.cudart().cudaProfilerStop()
     d.barrier()
-    ck = clocks.stop()
+    ck = clocks.stop(t_begin, t_end)
     step_ms = [a.elapsed_time(b) for a, b in evs]
     t_step = d.max(float(np.mean(step_ms)))
     total_q = d.sum(float(nq))

@@ -68,6 +68,8 @@ struct gann_handle {
   int32_t* nav_adj = nullptr;
   int32_t* nav_map = nullptr;
   int32_t* counter = nullptr;        // [0]: work counter, [1..2]: error counts
+  uint32_t* vis = nullptr;           // per-warp visited-id tables
+  int64_t vis_slots = 0;
   int64_t device_bytes = 0;
   // reusable buffers of gann_search
   int64_t cap_q = 0, cap_out = 0;
@@ -97,7 +99,8 @@ struct gann_handle {
     for (void* p : {static_cast<void*>(codes), static_cast<void*>(pivots_t), static_cast<void*>(centroid),
                     static_cast<void*>(chunk_off), static_cast<void*>(piv4), static_cast<void*>(ncodes),
                     static_cast<void*>(nav_vecs), static_cast<void*>(nav_adj),
-                    static_cast<void*>(nav_map), static_cast<void*>(counter), static_cast<void*>(d_q),
+                    static_cast<void*>(nav_map), static_cast<void*>(counter), static_cast<void*>(vis),
+                    static_cast<void*>(d_q),
                     static_cast<void*>(d_nns), static_cast<void*>(d_dist), static_cast<void*>(d_found),
                     static_cast<void*>(d_hops), static_cast<void*>(d_adc)})
       if (p) cudaFree(p);
@@ -111,6 +114,22 @@ struct gann_handle {
 };
 
 namespace {
+
+// Visited-id tables for every warp the search kernels keep resident. The
+// search skips neighbours whose id is in its warp's table; the table is
+// cleared per query (by the kernel), so no state crosses queries or calls.
+cudaError_t alloc_vis(gann_handle* h) {
+  h->vis_slots = static_cast<int64_t>(h->sm_count) * gann::kVisWarpsPerSM;
+  const size_t bytes = sizeof(uint32_t) * (static_cast<size_t>(h->vis_slots) << gann::kVisBits);
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&h->vis), bytes);
+  if (e != cudaSuccess) {
+    h->vis = nullptr;
+    h->vis_slots = 0;
+    return e;
+  }
+  h->device_bytes += static_cast<int64_t>(bytes);
+  return cudaSuccess;
+}
 
 int load_records(gann_handle* h, const std::string& path) {
   HostIndex& hi = h->hi;
@@ -233,6 +252,7 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
     hi.nav_vecs.shrink_to_fit();
   }
   GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->counter), 4 * sizeof(int32_t)));
+  GANN_CUDA(alloc_vis(h));
   if ((rc = load_records(h, cfg->index_file))) return rc;
   if (cfg->layout < 0 || cfg->layout > 2) return set_error(GANN_EINVAL, "gann_open: layout must be 0, 1 or 2");
   if (cfg->layout != 1) {
@@ -288,6 +308,8 @@ gann::SearchArgs make_args(gann_handle* h, const float* q, int64_t nq, int32_t t
   a.adc = adc;
   a.qcounter = h->counter;
   a.err = h->counter + 1;
+  a.vis = h->vis;
+  a.vis_slots = h->vis_slots;
   return a;
 }
 
@@ -350,6 +372,7 @@ int open_device_impl(const gann_device_index* d, gann_handle* h) {
   if ((rc = dev_upload(h->centroid, hi.centroid.data(), hi.centroid.size(), h->device_bytes))) return rc;
   if ((rc = dev_upload(h->chunk_off, hi.chunk_offsets.data(), hi.chunk_offsets.size(), h->device_bytes))) return rc;
   GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->counter), 4 * sizeof(int32_t)));
+  GANN_CUDA(alloc_vis(h));
   DeviceIndex& ix = h->ix;
   ix.vecs = static_cast<const uint8_t*>(d->vectors);
   ix.adj = d->adjacency;

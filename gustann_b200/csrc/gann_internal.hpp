@@ -85,7 +85,17 @@ struct SearchArgs {
   uint32_t* adc = nullptr;         // nullable
   int32_t* qcounter = nullptr;     // work counter (zeroed before launch)
   int32_t* err = nullptr;          // [2]: capped queries, capped nav searches
+  // per-warp visited-id tables (nullable): vis_slots tables of 2^kVisBits ids,
+  // table i used by the warp with global warp index i
+  uint32_t* vis = nullptr;
+  int64_t vis_slots = 0;
 };
+
+// Visited-id table of one warp: 2^kVisBits slots (8 KB). A buffer of
+// sm_count * kVisWarpsPerSM tables covers every warp either kernel keeps
+// resident (at most 32 one-warp CTAs per SM in table mode).
+constexpr int kVisBits = 11;
+constexpr int kVisWarpsPerSM = 32;
 
 // Kernel launchers (gann_search.cu)
 cudaError_t launch_search(const DeviceIndex& ix, const SearchArgs& a, int dtype,

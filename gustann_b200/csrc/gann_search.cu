@@ -397,11 +397,17 @@ __global__ void gather_neighbour_codes(const uint32_t* __restrict__ adj, int adj
 // the merge and the top-k insert of the current node run while those loads are
 // in flight.
 //
-// A neighbour that is already in the pool would be dropped as a duplicate of
-// the pool copy (same id, hence same PQ distance), so its code row and ADC are
-// skipped when the membership table says so. The table is lossy but never
-// wrong in that direction: slot h(id) holds id only while id is in the pool
-// (written when it enters, cleared when it is pushed out past `ef`).
+// Neighbours whose ADC cannot change the pool are skipped, from two lossy id
+// tables that are never wrong in that direction:
+//  * the warp's visited table (global memory, L2-resident, cleared per query)
+//    holds ids evaluated earlier in this query. Such a node is either in the
+//    pool (a duplicate of the pool copy, same id and distance) or was dropped
+//    or pushed out while the pool was full; a full pool's last key never
+//    grows, so it would be dropped again.
+//  * the shared-memory membership table: slot h(id) holds id only while id is
+//    in the pool (written when it enters, cleared when it is pushed out).
+// The remaining neighbours are compacted to the low lanes, so a hop with at
+// most 32 of them runs one ADC pass instead of NPL.
 template <typename T, int NPL, int VP, int PIV>
 __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid, uint32_t entry,
                          const WarpSmem& s, const PivTab& piv, int lane, int pl) {
@@ -416,6 +422,13 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
   bool capped = false;
 
   for (int i = lane; i < fsz; i += kWarp) s.filt[i] = kPadId;
+  // this warp's visited table (none when the caller gave no buffer)
+  const int64_t wslot = static_cast<int64_t>(blockIdx.x) * (blockDim.x / kWarp) + threadIdx.x / kWarp;
+  uint32_t* const vis = a.vis != nullptr && wslot < a.vis_slots ? a.vis + (wslot << kVisBits) : nullptr;
+  auto vslot = [](uint32_t id) { return static_cast<int>((id * 0x9E3779B1u) >> (32 - kVisBits)); };
+  if (vis != nullptr)
+    for (int i = 4 * lane; i < (1 << kVisBits); i += 4 * kWarp)
+      *reinterpret_cast<uint4*>(vis + i) = make_uint4(kPadId, kPadId, kPadId, kPadId);
   float qv[VP];   // q'' = (q - c) + c, the lane's dims
 #pragma unroll
   for (int v = 0; v < VP; ++v) {
@@ -433,22 +446,45 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       break;
     }
     ++hops;
-    // code rows of the neighbours to evaluate: slot k of u's neighbour-code
-    // block (prefetched into L2 when u was chosen), else row nb[k] of `codes`
+    // neighbours to evaluate, compacted to lanes 0.. of pass 0, then pass 1
+    // (ids in candr, neighbour slots in hist until the merge reuses both)
+    uint32_t seen[NPL];
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) seen[k] = vis != nullptr && nb[k] != kPadId ? vis[vslot(nb[k])] : kPadId;
+    int cnt = 0;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      adc += __popc(__ballot_sync(kFull, nb[k] != kPadId));
+      const bool e = nb[k] != kPadId && seen[k] != nb[k] && s.filt[fslot(nb[k])] != nb[k];
+      const unsigned bm = __ballot_sync(kFull, e);
+      if (e) {
+        const int pos = cnt + __popc(bm & ((1u << lane) - 1u));
+        s.candr[pos] = static_cast<int>(nb[k]);
+        s.hist[pos] = lane + kWarp * k;
+      }
+      cnt += __popc(bm);
+    }
+    __syncwarp();
+    // their code rows: slot of u's neighbour-code block (prefetched into L2
+    // when u was chosen), else row id of `codes`; ids enter the visited table
     bool ok[NPL];
     const uint4* crow[NPL];
     uint4 c0[NPL], c1[NPL];
     const bool inl = ix.ncodes != nullptr;
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
-      adc += __popc(__ballot_sync(kFull, nb[k] != kPadId));
-      ok[k] = nb[k] != kPadId && s.filt[fslot(nb[k])] != nb[k];
+      const int j = lane + kWarp * k;
+      ok[k] = j < cnt;
+      nb[k] = ok[k] ? static_cast<uint32_t>(s.candr[j]) : kPadId;
+      const int slot = ok[k] ? s.hist[j] : 0;
       crow[k] = reinterpret_cast<const uint4*>(
-          inl ? ix.ncodes + (static_cast<size_t>(u) * ix.adj_stride + lane + kWarp * k) * ix.code_stride
+          inl ? ix.ncodes + (static_cast<size_t>(u) * ix.adj_stride + slot) * ix.code_stride
               : ix.codes + static_cast<size_t>(ok[k] ? nb[k] : 0) * ix.code_stride);
       c0[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
       c1[k] = (ok[k] && mw > 1) ? __ldg(crow[k] + 1) : make_uint4(0, 0, 0, 0);
+      if (ok[k] && vis != nullptr) vis[vslot(nb[k])] = nb[k];
     }
+    __syncwarp();
 
     // first unvisited pool entry; every entry before `pfirst` is visited
     int ppos = -1;

@@ -2,10 +2,12 @@
 
 `kernel_expansions` mirrors `traverse()` in gustann_b200/csrc/gann_search.cu
 step for step at warp-chunk granularity -- 64-bit candidate keys, the lossy
-pool-membership table and its hash, the "beyond the last entry" and duplicate
-drops, ranks by lower bound, the next node chosen before the merge, the
-histogram + prefix + high-to-low moves starting at the smallest survivor rank's
-chunk, and the first-unvisited lower bound -- so that changes to those
+pool-membership table and its hash, the per-query visited-id table (every
+evaluated id, never cleared within a query), the "beyond the last entry" and
+duplicate drops, ranks by lower bound, the next node chosen before the merge,
+the shifts from sorted survivor ranks + high-to-low moves starting at the
+smallest survivor rank's chunk, and the first-unvisited lower bound -- so that
+changes to those
 mechanics can be checked on the CPU against `reference_expansions`, a literal
 model of the reference's merge-path / 2L-cut / dedup / first-unvisited step
 (src/impl/pure_mem.cuh:314-419). Both return the sequence of expanded node ids;
@@ -99,16 +101,21 @@ def reference_expansions(entry, neighbours, adc, L, max_hops=1 << 14):
     return out, False
 
 
-def kernel_expansions(entry, neighbours, adc, L, max_hops=1 << 14):
-    """Model of the CUDA traverse(); returns the expanded ids."""
+def kernel_expansions(entry, neighbours, adc, L, max_hops=1 << 14, vis_bits=11):
+    """Model of the CUDA traverse(); returns the expanded ids. `vis_bits`
+    None models a search without the visited-id table."""
     pl = (L + WARP - 1) // WARP
     fbits = 5
     while (1 << fbits) < pl * WARP:
         fbits += 1
     filt = [0xFFFFFFFF] * (1 << fbits)
+    vis = [0xFFFFFFFF] * (1 << vis_bits) if vis_bits else None
 
     def fslot(i):
         return ((i * 0x9E3779B1) & 0xFFFFFFFF) >> (32 - fbits)
+
+    def vslot(i):
+        return ((i * 0x9E3779B1) & 0xFFFFFFFF) >> (32 - vis_bits)
 
     pool: list[int] = []              # sorted keys; bit 0 = unvisited
     pfirst = 0
@@ -117,9 +124,12 @@ def kernel_expansions(entry, neighbours, adc, L, max_hops=1 << 14):
     for _ in range(max_hops):
         out.append(u)
         nb = list(neighbours(u))
-        ok = [filt[fslot(v)] != v for v in nb]
+        ok = [filt[fslot(v)] != v and (vis is None or vis[vslot(v)] != v) for v in nb]
         ev = [v for v, k in zip(nb, ok) if k]
         dsum = dict(zip(ev, adc(ev).tolist())) if ev else {}
+        if vis is not None:
+            for v in ev:
+                vis[vslot(v)] = v
         # first unvisited from the hint, chunk by chunk
         psize = len(pool)
         ppos = -1
