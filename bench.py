@@ -47,7 +47,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c1", choices=list(datagen.CONFIGS))
-    ap.add_argument("--n", type=int, default=0, help="override the number of base points")
+    ap.add_argument("--points", "--n", dest="n", type=int, default=0,
+                    help="override the number of base points (use --points under torchrun: its parser takes --n)")
     ap.add_argument("--nq", type=int, default=10000)
     ap.add_argument("--target", type=float, default=0.9)
     ap.add_argument("--efs", default="32,48,64,80,96,112,128,144,160,176,192,224,256,320,384,448,512,640,768,1024")
