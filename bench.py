@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--cache", default=os.environ.get("GANN_BENCH_CACHE", "/tmp/gann_bench"))
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--split-records", action="store_true",
+                    help="N>1: each rank holds 1/N of the node records and reads the others over NVLink")
     return ap.parse_args()
 
 
@@ -328,7 +330,10 @@ def config_json(args, spec, ef, rec):
                         f"{spec.kind}-like mixture ({spec.centers} centers), R=64, PQ M=32, pivot graph, "
                         f"{args.nq} queries/rank, top-{TOPK}",
             "ef_search": ef, "recall_at_10": rec, "recall_target": args.target, "queries_per_rank": args.nq,
-            "l2_flush": "not needed: index (>6 GB) larger than L2", "parallelism": f"query shards x{args.gpus}"}
+            "l2_flush": "not needed: index (>6 GB) larger than L2",
+            "parallelism": f"query shards x{args.gpus}" + (f", records split x{args.gpus}"
+                                                            if getattr(args, "split_records", False) and args.gpus > 1
+                                                            else "")}
 
 
 def run_ours(args, d: Dist):
@@ -339,7 +344,14 @@ def run_ours(args, d: Dist):
     Q = datagen.as_float_queries(datagen.query_vectors(spec, args.nq, device="cuda", offset=d.rank))
     gt = ground_truth(spec, Q)
     g = GustANN(spec.dtype, device=dev)
-    g.init_pure_mem(GustANNConfig(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"]), True)
+    cfg = GustANNConfig(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"])
+    split = args.split_records and d.world > 1
+    if split:
+        from gustann_b200.sharding import exchange_parts
+        g.init_pure_mem(cfg, True, part_count=d.world, part_index=d.rank)
+        exchange_parts(g, d.rank, d.world)
+    else:
+        g.init_pure_mem(cfg, True)
 
     efs = [int(x) for x in args.efs.split(",")]
     sweep = []
@@ -431,6 +443,7 @@ def run_ours(args, d: Dist):
                "data": "synthetic", "config": config_json(args, spec, ef, rec), "e2e": e2e,
                "roofline": roof, "cpu_baseline": cpu, "clocks": ck, "gpu_launches": args.steps,
                "recall_sweep": sweep}
+    d.barrier()          # split records: peers read this rank's range until every rank is done
     g.close()
     return out
 

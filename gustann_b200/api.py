@@ -21,13 +21,14 @@ from .formats import FLOAT, UINT8
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_lib", "libgann.so")
 
+PART_BLOB_BYTES = 512   # GANN_PART_BLOB_BYTES
 GANN_OK, GANN_EINVAL, GANN_EIO, GANN_ENOMEM, GANN_ECUDA, GANN_ETIMEDOUT, GANN_EUNSUPPORTED, GANN_ESTATE = range(8)
 STATUS_NAMES = ["OK", "EINVAL", "EIO", "ENOMEM", "ECUDA", "ETIMEDOUT", "EUNSUPPORTED", "ESTATE"]
 
 # Every symbol include/gann.h declares.
 EXPORTS = ["gann_open", "gann_open_device", "gann_search", "gann_search_device", "gann_close", "gann_last_error",
            "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample", "gann_set_option",
-           "gann_search_noalloc"]
+           "gann_search_noalloc", "gann_part_export", "gann_part_attach"]
 GANN_OPT_ADC_MODE, GANN_OPT_PIVOT_WARPS, GANN_OPT_NEIGHBOUR_CODES = 1, 2, 3
 LAYOUT_AUTO, LAYOUT_SEPARATE, LAYOUT_NEIGHBOUR_CODES = 0, 1, 2
 ADC_AUTO, ADC_TABLE, ADC_PIVOT = 0, 1, 2
@@ -43,7 +44,8 @@ class GustANNError(RuntimeError):
 class _Config(C.Structure):
     _fields_ = [("index_file", C.c_char_p), ("pq_file_prefix", C.c_char_p), ("nav_graph_prefix", C.c_char_p),
                 ("dtype", C.c_int32), ("use_gpu_mem", C.c_int32), ("device", C.c_int32),
-                ("layout", C.c_int32), ("reserved", C.c_int32 * 4)]
+                ("layout", C.c_int32), ("part_count", C.c_int32), ("part_index", C.c_int32),
+                ("reserved", C.c_int32 * 2)]
 
 
 class _Stats(C.Structure):
@@ -84,6 +86,8 @@ def _load() -> C.CDLL:
     lib.gann_pivot_sample.argtypes = [i64, i64, C.c_uint32, ip]
     lib.gann_set_option.argtypes = [vp, i32, i64]
     lib.gann_search_noalloc.argtypes = [C.POINTER(_DeviceIndex), vp, i64, i32, i32, vp, vp, vp, vp]
+    lib.gann_part_export.argtypes = [vp, vp, i64]
+    lib.gann_part_attach.argtypes = [vp, i32, C.c_char_p, i64]
     for name in EXPORTS:
         if name != "gann_last_error":
             getattr(lib, name).restype = C.c_int
@@ -136,12 +140,16 @@ class GustANN:
         self.dim = 0
 
     # --------------------------------------------------------------- init
-    def init_pure_mem(self, config: GustANNConfig, use_gpu_mem: bool) -> None:
-        """``GustANN::init_pure_mem`` (``src/ssd_search.cu:108-112``)."""
+    def init_pure_mem(self, config: GustANNConfig, use_gpu_mem: bool, part_count: int = 0,
+                      part_index: int = 0) -> None:
+        """``GustANN::init_pure_mem`` (``src/ssd_search.cu:108-112``). With
+        ``part_count`` > 1 the node records are split by id range and this
+        handle loads range ``part_index`` (-1: every range, on this device);
+        other processes' ranges are added with :meth:`attach_part`."""
         self.close()
         cfg = _Config(config.index_file.encode(), config.pq_file_prefix.encode(),
                       (config.nav_graph_prefix or "").encode(), self.data_type, int(bool(use_gpu_mem)),
-                      self.device, self.layout)
+                      self.device, self.layout, part_count, part_index)
         h = C.c_void_p()
         _check(lib.gann_open(C.byref(cfg), C.byref(h)))
         self._h = h
@@ -230,6 +238,22 @@ class GustANN:
         e = np.zeros(q.shape[0], np.int32)
         _check(lib.gann_probe_entry(self._h, _ptr(q), q.shape[0], _ptr(s), _ptr(e)))
         return s, e
+
+    def export_part(self) -> bytes:
+        """``gann_part_export``: an opaque blob naming this handle's record
+        range for :meth:`attach_part` in another process."""
+        self._need()
+        buf = C.create_string_buffer(PART_BLOB_BYTES)
+        _check(lib.gann_part_export(self._h, buf, PART_BLOB_BYTES))
+        return buf.raw
+
+    def attach_part(self, part: int, blob: bytes) -> None:
+        """``gann_part_attach``: map record range ``part`` exported by another
+        process (peer access over NVLink)."""
+        self._need()
+        if len(blob) < PART_BLOB_BYTES:
+            raise GustANNError(GANN_EINVAL, "blob too short")
+        _check(lib.gann_part_attach(self._h, part, blob, PART_BLOB_BYTES))
 
     def set_option(self, option: int, value: int) -> None:
         """``gann_set_option``: ADC mode (0 auto, 1 table, 2 pivot) or pivot warps."""

@@ -70,6 +70,16 @@ struct gann_handle {
   int32_t* counter = nullptr;        // [0]: work counter, [1..2]: error counts
   uint32_t* vis = nullptr;           // per-warp visited-id tables
   int64_t vis_slots = 0;
+  const uint8_t* ncodes_on = nullptr;  // ix.ncodes value when the copy is in use
+  // split records (part_count > 1): this handle's ranges, or ranges mapped
+  // from other processes (pattached)
+  int32_t part_count = 0, part_index = 0;
+  int32_t part_ncodes = 0;           // every range carries neighbour codes
+  uint8_t* pvecs[gann::kMaxParts] = {};
+  uint32_t* padj[gann::kMaxParts] = {};
+  uint8_t* pncodes[gann::kMaxParts] = {};
+  bool ppresent[gann::kMaxParts] = {};
+  bool pattached[gann::kMaxParts] = {};
   int64_t device_bytes = 0;
   // reusable buffers of gann_search
   int64_t cap_q = 0, cap_out = 0;
@@ -104,6 +114,16 @@ struct gann_handle {
                     static_cast<void*>(d_nns), static_cast<void*>(d_dist), static_cast<void*>(d_found),
                     static_cast<void*>(d_hops), static_cast<void*>(d_adc)})
       if (p) cudaFree(p);
+    for (int p = 0; p < gann::kMaxParts; ++p) {
+      for (void* q : {static_cast<void*>(pvecs[p]), static_cast<void*>(padj[p]), static_cast<void*>(pncodes[p])}) {
+        if (!q) continue;
+        if (pattached[p]) cudaIpcCloseMemHandle(q);
+        else cudaFree(q);
+      }
+      pvecs[p] = nullptr;
+      padj[p] = nullptr;
+      pncodes[p] = nullptr;
+    }
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     if (stream) cudaStreamDestroy(stream);
@@ -171,6 +191,79 @@ int load_records(gann_handle* h, const std::string& path) {
   return GANN_OK;
 }
 
+// Split records: id range p = [p << shift, (p + 1) << shift) of the index,
+// with its own vector, adjacency and (when it fits) neighbour-code arrays.
+int load_part(gann_handle* h, const gann_config* cfg, int p, bool with_ncodes) {
+  HostIndex& hi = h->hi;
+  DeviceIndex& ix = h->ix;
+  const int64_t first = static_cast<int64_t>(p) << ix.part_shift;
+  const int64_t rows = std::max<int64_t>(0, std::min<int64_t>(hi.num_points - first, int64_t(1) << ix.part_shift));
+  h->ppresent[p] = true;
+  if (rows == 0) return GANN_OK;
+  const int64_t vs = ix.vec_stride;
+  const int32_t as = ix.adj_stride;
+  GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->pvecs[p]), static_cast<size_t>(rows) * vs));
+  GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->padj[p]), static_cast<size_t>(rows) * as * 4));
+  h->device_bytes += rows * (vs + 4 * as);
+  const int64_t blk = 1 << 20;
+  std::vector<uint8_t> sv(static_cast<size_t>(std::min(blk, rows)) * vs);
+  std::vector<uint32_t> sa(static_cast<size_t>(std::min(blk, rows)) * as);
+  std::string msg;
+  for (int64_t r = 0; r < rows; r += blk) {
+    const int64_t c = std::min(blk, rows - r);
+    int rc = gann::relayout_records(cfg->index_file, hi, first + r, c, sv.data(), vs, sa.data(), as, msg);
+    if (rc) return set_error(rc, msg);
+    GANN_CUDA(cudaMemcpy(h->pvecs[p] + r * vs, sv.data(), static_cast<size_t>(c) * vs, cudaMemcpyHostToDevice));
+    GANN_CUDA(cudaMemcpy(h->padj[p] + r * as, sa.data(), static_cast<size_t>(c) * as * 4, cudaMemcpyHostToDevice));
+  }
+  if (with_ncodes) {
+    const size_t bytes = static_cast<size_t>(rows) * as * ix.code_stride;
+    GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->pncodes[p]), bytes));
+    h->device_bytes += static_cast<int64_t>(bytes);
+    GANN_CUDA(gann::launch_gather_neighbour_codes(h->padj[p], as, ix.degree, ix.codes, ix.code_stride, rows,
+                                                  h->pncodes[p], h->stream));
+    GANN_CUDA(cudaStreamSynchronize(h->stream));
+  }
+  ix.part_vecs[p] = h->pvecs[p];
+  ix.part_adj[p] = h->padj[p];
+  ix.part_ncodes[p] = h->pncodes[p];
+  return GANN_OK;
+}
+
+int load_parts(gann_handle* h, const gann_config* cfg) {
+  HostIndex& hi = h->hi;
+  DeviceIndex& ix = h->ix;
+  int shift = 0;
+  while ((static_cast<int64_t>(h->part_count) << shift) < hi.num_points) ++shift;
+  ix.nparts = h->part_count;
+  ix.part_shift = shift;
+  ix.vec_stride = gann::round_up(hi.dim, 32) * hi.elem;
+  ix.adj_stride = static_cast<int32_t>(gann::round_up(hi.max_m0, 4));
+  // neighbour codes per range, on the same rule as the single layout,
+  // applied to the ranges this device holds
+  const int nown = h->part_index < 0 ? h->part_count : 1;
+  const size_t bytes = (static_cast<size_t>(nown) << shift) * ix.adj_stride * ix.code_stride;
+  size_t free_b = 0, total_b = 0;
+  GANN_CUDA(cudaMemGetInfo(&free_b, &total_b));
+  const bool fits = bytes <= total_b / 4 && bytes + (size_t(1) << 30) < free_b;
+  if (cfg->layout == 2 && !fits)
+    return set_error(GANN_ENOMEM, "gann_open: the neighbour-code copy does not fit in device memory");
+  const bool with_ncodes = cfg->layout != 1 && fits;
+  h->part_ncodes = with_ncodes ? 1 : 0;
+  for (int p = 0; p < h->part_count; ++p) {
+    if (h->part_index >= 0 && p != h->part_index) continue;
+    int rc = load_part(h, cfg, p, with_ncodes);
+    if (rc) return rc;
+  }
+  if (with_ncodes) {
+    // any non-null pointer marks the layout; rows are addressed per range
+    for (int p = 0; p < h->part_count && !h->ncodes_on; ++p) h->ncodes_on = h->pncodes[p];
+    if (!h->ncodes_on) h->ncodes_on = reinterpret_cast<const uint8_t*>(ix.codes);
+    ix.ncodes = h->ncodes_on;
+  }
+  return GANN_OK;
+}
+
 int upload_pivot_table(gann_handle* h) {
   std::vector<float> tab;
   const int w = gann::make_pivot_table(h->hi.pivots_t, h->hi.chunk_offsets, static_cast<int>(h->hi.dim), tab);
@@ -191,6 +284,15 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
   h->device = cfg->device;
   h->dtype = cfg->dtype;
   h->host_records = cfg->use_gpu_mem == 0;
+  if (cfg->layout < 0 || cfg->layout > 2) return set_error(GANN_EINVAL, "gann_open: layout must be 0, 1 or 2");
+  if (cfg->part_count < 0 || cfg->part_count > gann::kMaxParts)
+    return set_error(GANN_EINVAL, "gann_open: part_count must be 0..8");
+  h->part_count = cfg->part_count > 1 ? cfg->part_count : 0;
+  h->part_index = h->part_count ? cfg->part_index : 0;
+  if (h->part_count && (h->part_index < -1 || h->part_index >= h->part_count))
+    return set_error(GANN_EINVAL, "gann_open: part_index must be -1..part_count-1");
+  if (h->part_count && h->host_records)
+    return set_error(GANN_EUNSUPPORTED, "gann_open: split records need use_gpu_mem = 1");
 
   // parse and validate every file before touching the GPU
   HostIndex& hi = h->hi;
@@ -253,8 +355,8 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
   }
   GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->counter), 4 * sizeof(int32_t)));
   GANN_CUDA(alloc_vis(h));
+  if (h->part_count) return load_parts(h, cfg);
   if ((rc = load_records(h, cfg->index_file))) return rc;
-  if (cfg->layout < 0 || cfg->layout > 2) return set_error(GANN_EINVAL, "gann_open: layout must be 0, 1 or 2");
   if (cfg->layout != 1) {
     // neighbour codes next to the adjacency: built on the GPU from the records
     // just loaded (in host-record mode the adjacency is read through UVA)
@@ -271,6 +373,7 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
                                                     hi.num_points, h->ncodes, h->stream));
       GANN_CUDA(cudaStreamSynchronize(h->stream));
       ix.ncodes = h->ncodes;
+      h->ncodes_on = h->ncodes;
     }
   }
   return GANN_OK;
@@ -281,6 +384,9 @@ int check_search_args(gann_handle* h, int64_t nq, int32_t topk, int32_t ef) {
   if (nq < 0 || nq >= (int64_t(1) << 31) - (int64_t(1) << 24))
     return set_error(GANN_EINVAL, "search: query count out of range");
   if (topk < 1 || topk > ef) return set_error(GANN_EINVAL, "search: need 1 <= topk <= ef_search");
+  for (int p = 0; p < h->part_count; ++p)
+    if (!h->ppresent[p])
+      return set_error(GANN_ESTATE, "search: record range " + std::to_string(p) + " is not attached");
   if (h->hi.dim > 1024) return set_error(GANN_EUNSUPPORTED, "search: dimension above 1024");
   if (ef > gann::search_max_ef())
     return set_error(GANN_EUNSUPPORTED, "search: ef_search above " + std::to_string(gann::search_max_ef()));
@@ -445,6 +551,88 @@ int gann_close(gann_handle* h) {
 
 const char* gann_last_error(void) { return g_last_error.c_str(); }
 
+namespace {
+// Content of a gann_part_export blob.
+struct PartBlob {
+  uint32_t magic, version;
+  int32_t part, part_count, part_shift, has_ncodes;
+  int64_t num_points, rows, vec_stride;
+  int32_t adj_stride, code_stride;
+  cudaIpcMemHandle_t vecs, adj, ncodes;
+};
+constexpr uint32_t kBlobMagic = 0x47414e50u;  // "GANP"
+static_assert(sizeof(PartBlob) <= GANN_PART_BLOB_BYTES, "blob too large");
+
+int64_t part_rows(const gann_handle* h, int p) {
+  const int64_t first = static_cast<int64_t>(p) << h->ix.part_shift;
+  return std::max<int64_t>(0, std::min<int64_t>(h->hi.num_points - first, int64_t(1) << h->ix.part_shift));
+}
+}  // namespace
+
+int gann_part_export(gann_handle* h, void* blob, int64_t blob_bytes) {
+  if (!h || !blob || blob_bytes < GANN_PART_BLOB_BYTES) return set_error(GANN_EINVAL, "gann_part_export: bad argument");
+  if (h->part_count < 2 || h->part_index < 0)
+    return set_error(GANN_ESTATE, "gann_part_export: the handle does not own one record range");
+  const int p = h->part_index;
+  PartBlob b;
+  std::memset(&b, 0, sizeof(b));
+  b.magic = kBlobMagic;
+  b.version = GANN_ABI_VERSION;
+  b.part = p;
+  b.part_count = h->part_count;
+  b.part_shift = h->ix.part_shift;
+  b.has_ncodes = h->part_ncodes;
+  b.num_points = h->hi.num_points;
+  b.rows = part_rows(h, p);
+  b.vec_stride = h->ix.vec_stride;
+  b.adj_stride = h->ix.adj_stride;
+  b.code_stride = h->ix.code_stride;
+  GANN_CUDA(cudaSetDevice(h->device));
+  if (b.rows > 0) {
+    GANN_CUDA(cudaIpcGetMemHandle(&b.vecs, h->pvecs[p]));
+    GANN_CUDA(cudaIpcGetMemHandle(&b.adj, h->padj[p]));
+    if (h->pncodes[p]) GANN_CUDA(cudaIpcGetMemHandle(&b.ncodes, h->pncodes[p]));
+  }
+  std::memset(blob, 0, GANN_PART_BLOB_BYTES);
+  std::memcpy(blob, &b, sizeof(b));
+  return GANN_OK;
+}
+
+int gann_part_attach(gann_handle* h, int32_t part, const void* blob, int64_t blob_bytes) {
+  if (!h || !blob || blob_bytes < GANN_PART_BLOB_BYTES) return set_error(GANN_EINVAL, "gann_part_attach: bad argument");
+  PartBlob b;
+  std::memcpy(&b, blob, sizeof(b));
+  if (b.magic != kBlobMagic || b.version != GANN_ABI_VERSION)
+    return set_error(GANN_EINVAL, "gann_part_attach: not a record-range blob of this library");
+  if (h->part_count < 2 || part < 0 || part >= h->part_count || b.part != part)
+    return set_error(GANN_EINVAL, "gann_part_attach: range index out of range or not the blob's range");
+  if (h->ppresent[part]) return set_error(GANN_ESTATE, "gann_part_attach: the range is already present");
+  if (b.part_count != h->part_count || b.part_shift != h->ix.part_shift || b.num_points != h->hi.num_points ||
+      b.rows != part_rows(h, part) || b.vec_stride != h->ix.vec_stride || b.adj_stride != h->ix.adj_stride ||
+      b.code_stride != h->ix.code_stride || b.has_ncodes != h->part_ncodes)
+    return set_error(GANN_EINVAL, "gann_part_attach: the range was exported from a different index or layout");
+  GANN_CUDA(cudaSetDevice(h->device));
+  h->pattached[part] = true;
+  if (b.rows > 0) {
+    void* v = nullptr;
+    void* a = nullptr;
+    void* c = nullptr;
+    GANN_CUDA(cudaIpcOpenMemHandle(&v, b.vecs, cudaIpcMemLazyEnablePeerAccess));
+    h->pvecs[part] = static_cast<uint8_t*>(v);
+    GANN_CUDA(cudaIpcOpenMemHandle(&a, b.adj, cudaIpcMemLazyEnablePeerAccess));
+    h->padj[part] = static_cast<uint32_t*>(a);
+    if (b.has_ncodes) {
+      GANN_CUDA(cudaIpcOpenMemHandle(&c, b.ncodes, cudaIpcMemLazyEnablePeerAccess));
+      h->pncodes[part] = static_cast<uint8_t*>(c);
+    }
+  }
+  h->ix.part_vecs[part] = h->pvecs[part];
+  h->ix.part_adj[part] = h->padj[part];
+  h->ix.part_ncodes[part] = h->pncodes[part];
+  h->ppresent[part] = true;
+  return GANN_OK;
+}
+
 int gann_set_option(gann_handle* h, int32_t option, int64_t value) {
   if (!h) return set_error(GANN_EINVAL, "gann_set_option: null handle");
   switch (option) {
@@ -461,9 +649,9 @@ int gann_set_option(gann_handle* h, int32_t option, int64_t value) {
       return GANN_OK;
     case GANN_OPT_NEIGHBOUR_CODES:
       if (value != 0 && value != 1) return set_error(GANN_EINVAL, "gann_set_option: neighbour codes must be 0 or 1");
-      if (value == 1 && !h->ncodes)
+      if (value == 1 && !h->ncodes_on)
         return set_error(GANN_ESTATE, "gann_set_option: the handle was opened without the neighbour-code copy");
-      h->ix.ncodes = value ? h->ncodes : nullptr;
+      h->ix.ncodes = value ? h->ncodes_on : nullptr;
       return GANN_OK;
     default:
       return set_error(GANN_EINVAL, "gann_set_option: unknown option");

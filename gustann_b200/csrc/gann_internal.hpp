@@ -43,6 +43,8 @@ struct HostIndex {
 };
 
 // Device layout: records split into aligned vector rows and adjacency rows.
+constexpr int kMaxParts = 8;
+
 struct DeviceIndex {
   const uint8_t* vecs = nullptr;     // [N x vec_stride]
   const uint32_t* adj = nullptr;     // [N x adj_stride] u32, kPadId after deg
@@ -70,7 +72,15 @@ struct DeviceIndex {
   // each code_stride bytes (nullptr when the index keeps codes separate only)
   const uint8_t* ncodes = nullptr;
   int32_t adc_mode = 0;     // 0 auto, 1 table, 2 pivot
-  int32_t piv_warps = 0;    // 0 = as many as fit (<= 24)
+  int32_t piv_warps = 0;    // 0 = as many as fit (<= 20)
+  // records split by id (nparts > 1): part p holds ids [p << part_shift,
+  // (p + 1) << part_shift) in its own arrays (possibly another GPU's memory,
+  // reached through peer pointers); vecs/adj/ncodes above are then unused
+  int32_t nparts = 0;
+  int32_t part_shift = 0;
+  const uint8_t* part_vecs[kMaxParts] = {};
+  const uint32_t* part_adj[kMaxParts] = {};
+  const uint8_t* part_ncodes[kMaxParts] = {};
 };
 
 struct SearchArgs {

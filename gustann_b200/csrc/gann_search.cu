@@ -292,17 +292,9 @@ struct WarpSmem {
   uint64_t* cand;
   int* candr;
   int* hist;       // survivor ranks in key order (merge)
-  uint32_t* filt;   // lossy id -> pool-membership table (see traverse)
   float* topd;
   int* topi;
 };
-
-// Pool-membership table size: a power of two >= the pool capacity.
-__host__ __device__ inline int filt_bits(int pl) {
-  int b = 5;
-  while ((1 << b) < pl * kWarp) ++b;
-  return b;
-}
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
@@ -324,7 +316,6 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
   unsigned char* cand = take(sizeof(uint64_t) * npl * kWarp);
   unsigned char* candr = take(sizeof(int) * npl * kWarp);
   unsigned char* hist = take(sizeof(int) * npl * kWarp);
-  unsigned char* filt = take(sizeof(uint32_t) << filt_bits(pl));
   unsigned char* topd = take(sizeof(float) * topk);
   unsigned char* topi = take(sizeof(int) * topk);
   if (w) {
@@ -336,11 +327,31 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
     w->cand = reinterpret_cast<uint64_t*>(cand);
     w->candr = reinterpret_cast<int*>(candr);
     w->hist = reinterpret_cast<int*>(hist);
-    w->filt = reinterpret_cast<uint32_t*>(filt);
     w->topd = reinterpret_cast<float*>(topd);
     w->topi = reinterpret_cast<int*>(topi);
   }
   return off;
+}
+
+// Addresses of node u's adjacency row, vector and neighbour-code block, in
+// the single arrays or, with split records, in the arrays of u's part.
+__device__ __forceinline__ const uint32_t* adj_row(const DeviceIndex& ix, uint32_t u) {
+  if (ix.nparts > 1)
+    return ix.part_adj[u >> ix.part_shift] +
+           static_cast<size_t>(u & ((1u << ix.part_shift) - 1u)) * ix.adj_stride;
+  return ix.adj + static_cast<size_t>(u) * ix.adj_stride;
+}
+__device__ __forceinline__ const uint8_t* vec_row(const DeviceIndex& ix, uint32_t u) {
+  if (ix.nparts > 1)
+    return ix.part_vecs[u >> ix.part_shift] +
+           static_cast<size_t>(u & ((1u << ix.part_shift) - 1u)) * ix.vec_stride;
+  return ix.vecs + static_cast<size_t>(u) * ix.vec_stride;
+}
+__device__ __forceinline__ const uint8_t* ncode_row(const DeviceIndex& ix, uint32_t u) {
+  const size_t row = static_cast<size_t>(ix.adj_stride) * ix.code_stride;
+  if (ix.nparts > 1)
+    return ix.part_ncodes[u >> ix.part_shift] + static_cast<size_t>(u & ((1u << ix.part_shift) - 1u)) * row;
+  return ix.ncodes + static_cast<size_t>(u) * row;
 }
 
 // Neighbour ids (padding = kPadId) and the vector elements lane l owns
@@ -351,21 +362,21 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
 template <typename T, int NPL, int VP>
 __device__ __forceinline__ void load_node(const DeviceIndex& ix, uint32_t u, int lane, uint32_t (&nb)[NPL],
                                           float (&xv)[VP]) {
-  const uint32_t* arow = ix.adj + static_cast<size_t>(u) * ix.adj_stride;
+  const uint32_t* arow = adj_row(ix, u);
 #pragma unroll
   for (int k = 0; k < NPL; ++k) {
     const int e = lane + kWarp * k;
     nb[k] = e < ix.degree ? __ldg(arow + e) : kPadId;
   }
   if (ix.ncodes != nullptr) {
-    const uint8_t* crow = ix.ncodes + static_cast<size_t>(u) * ix.adj_stride * ix.code_stride;
+    const uint8_t* crow = ncode_row(ix, u);
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
       const int e = lane + kWarp * k;
       if (e < ix.degree) asm volatile("prefetch.global.L2 [%0];" ::"l"(crow + static_cast<size_t>(e) * ix.code_stride));
     }
   }
-  const T* xr = reinterpret_cast<const T*>(ix.vecs) + static_cast<size_t>(u) * (ix.vec_stride / sizeof(T));
+  const T* xr = reinterpret_cast<const T*>(vec_row(ix, u));
 #pragma unroll
   for (int v = 0; v < VP; ++v) {
     const int i = lane + kWarp * v;
@@ -397,31 +408,26 @@ __global__ void gather_neighbour_codes(const uint32_t* __restrict__ adj, int adj
 // the merge and the top-k insert of the current node run while those loads are
 // in flight.
 //
-// Neighbours whose ADC cannot change the pool are skipped, from two lossy id
-// tables that are never wrong in that direction:
-//  * the warp's visited table (global memory, L2-resident, cleared per query)
-//    holds ids evaluated earlier in this query. Such a node is either in the
-//    pool (a duplicate of the pool copy, same id and distance) or was dropped
-//    or pushed out while the pool was full; a full pool's last key never
-//    grows, so it would be dropped again.
-//  * the shared-memory membership table: slot h(id) holds id only while id is
-//    in the pool (written when it enters, cleared when it is pushed out).
-// The remaining neighbours are compacted to the low lanes, so a hop with at
-// most 32 of them runs one ADC pass instead of NPL.
+// Neighbours whose ADC cannot change the pool are skipped: the warp's visited
+// table (2^kVisBits ids in global memory, L2-resident, cleared per query) is a
+// lossy direct-mapped set of the ids evaluated earlier in this query, never
+// wrong in that direction. Such a node is either in the pool (a duplicate of
+// the pool copy, same id and distance) or was dropped or pushed out while the
+// pool was full; a full pool's last key never grows, so it would be dropped
+// again. The remaining neighbours are compacted to the low lanes, so a hop
+// with at most 32 of them runs one ADC pass instead of NPL. (Without a table,
+// e.g. gann_search_noalloc, every neighbour is evaluated; duplicates of pool
+// entries are then dropped by the rank search.)
 template <typename T, int NPL, int VP, int PIV>
 __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid, uint32_t entry,
                          const WarpSmem& s, const PivTab& piv, int lane, int pl) {
   const int dim = ix.dim, M = ix.chunks, L = a.ef, topk = a.topk;
   const int mw = ix.code_stride >> 4;
-  const int fbits = filt_bits(pl);
-  const int fsz = 1 << fbits;
-  auto fslot = [fbits](uint32_t id) { return static_cast<int>((id * 0x9E3779B1u) >> (32 - fbits)); };
   int psize = 0, tcnt = 0, pfirst = 0;
   uint32_t hops = 0, adc = 0;
   uint32_t u = entry;
   bool capped = false;
 
-  for (int i = lane; i < fsz; i += kWarp) s.filt[i] = kPadId;
   // this warp's visited table (none when the caller gave no buffer)
   const int64_t wslot = static_cast<int64_t>(blockIdx.x) * (blockDim.x / kWarp) + threadIdx.x / kWarp;
   uint32_t* const vis = a.vis != nullptr && wslot < a.vis_slots ? a.vis + (wslot << kVisBits) : nullptr;
@@ -455,7 +461,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
       adc += __popc(__ballot_sync(kFull, nb[k] != kPadId));
-      const bool e = nb[k] != kPadId && seen[k] != nb[k] && s.filt[fslot(nb[k])] != nb[k];
+      const bool e = nb[k] != kPadId && seen[k] != nb[k];
       const unsigned bm = __ballot_sync(kFull, e);
       if (e) {
         const int pos = cnt + __popc(bm & ((1u << lane) - 1u));
@@ -478,7 +484,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       nb[k] = ok[k] ? static_cast<uint32_t>(s.candr[j]) : kPadId;
       const int slot = ok[k] ? s.hist[j] : 0;
       crow[k] = reinterpret_cast<const uint4*>(
-          inl ? ix.ncodes + (static_cast<size_t>(u) * ix.adj_stride + slot) * ix.code_stride
+          inl ? ncode_row(ix, u) + static_cast<size_t>(slot) * ix.code_stride
               : ix.codes + static_cast<size_t>(ok[k] ? nb[k] : 0) * ix.code_stride);
       c0[k] = ok[k] ? __ldg(crow[k]) : make_uint4(0, 0, 0, 0);
       c1[k] = (ok[k] && mw > 1) ? __ldg(crow[k] + 1) : make_uint4(0, 0, 0, 0);
@@ -660,7 +666,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
         if (lane + kWarp * k < S) s.hist[cpos[k] - cr[k]] = cr[k];
       __syncwarp();
       // moves, four chunks at a time from the last one down (an entry only moves
-      // right); entries pushed past `ef` leave the pool and the membership table.
+      // right); entries pushed past `ef` leave the pool.
       // The shift of entry i is an upper bound in hist, found by power-of-two
       // steps with the four chunks' searches interleaved.
       const int j0 = rmin >> 5;
@@ -693,10 +699,6 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
         for (int g = 0; g < 4; ++g) {
           if (dst[g] < L) {
             s.pool[dst[g]] = v[g];
-          } else if (dst[g] != INT_MAX) {
-            const uint32_t id = static_cast<uint32_t>(v[g]) >> 1;
-            const int sl = fslot(id);
-            if (s.filt[sl] == id) s.filt[sl] = kPadId;
           }
         }
         __syncwarp();
@@ -705,8 +707,6 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       for (int k = 0; k < NPL; ++k) {
         if (cpos[k] < L) {
           s.pool[cpos[k]] = ck[k];
-          const uint32_t id = static_cast<uint32_t>(ck[k]) >> 1;
-          s.filt[fslot(id)] = id;
         }
       }
       // a next node taken from the pool in front of every survivor keeps its

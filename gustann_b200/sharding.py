@@ -59,3 +59,19 @@ def gather_results(n: int, topk: int, lo: int, nns, dst, found, device="cpu"):
     assert bool((full[:, 2 * topk + 1] == 1).all()), "a rank returned fewer rows than its slice"
     return (full[:, :topk].numpy().astype(np.int32), full[:, topk:2 * topk].numpy().astype(np.float32),
             full[:, 2 * topk].numpy().astype(np.int32))
+
+
+def exchange_parts(handle, rank: int, world: int) -> None:
+    """Split records (``init_pure_mem(..., part_count=world, part_index=rank)``):
+    give every rank every other rank's record range. Each rank exports its own
+    range (``gann_part_export``), the blobs are all-gathered (a collective:
+    every rank calls this once, after opening and before its first search), and
+    each rank attaches the others (``gann_part_attach``). Ranks must keep their
+    handles open while any rank still searches, because the others read their
+    ranges through those mappings."""
+    blob = handle.export_part()
+    blobs = [None] * world
+    dist.all_gather_object(blobs, (rank, blob))
+    for src, b in blobs:
+        if src != rank:
+            handle.attach_part(src, b)

@@ -57,6 +57,20 @@ typedef enum { GANN_UINT8 = 0, GANN_FLOAT = 1 } gann_dtype;
  *                     contiguous record). Auto builds the copy when it takes at
  *                     most a quarter of the device's memory. No counterpart in
  *                     the reference, which keeps one code array.
+ *   part_count        0 or 1: every node record on this device. k > 1 (<= 8):
+ *                     records split by id into k ranges of 2^s ids (the
+ *                     smallest s with k * 2^s >= N), one range per device;
+ *                     PQ codes, pivots and the nav graph stay whole on every
+ *                     device. A hop reads its node's record from the owner's
+ *                     HBM through a peer pointer (NVLink). The reference's
+ *                     scale-out plan for a 1B index (records partitioned by
+ *                     id range, queries sharded); the reference build itself
+ *                     has no multi-GPU search.
+ *   part_index        the range this handle loads (0..part_count-1); the other
+ *                     ranges are attached with gann_part_attach before the
+ *                     first search. -1 loads every range into its own
+ *                     allocation on this device (single-device use of the
+ *                     split addressing, e.g. for tests).
  */
 typedef struct {
   const char* index_file;
@@ -66,7 +80,9 @@ typedef struct {
   int32_t use_gpu_mem;
   int32_t device;
   int32_t layout;
-  int32_t reserved[4];
+  int32_t part_count;
+  int32_t part_index;
+  int32_t reserved[2];
 } gann_config;
 
 /* Replaces gustann::GustANNStats (src/ssd_search.hpp:25-27) and adds the
@@ -185,6 +201,19 @@ int gann_open_device(const gann_device_index* desc, gann_handle** out);
 int gann_search_noalloc(const gann_device_index* desc, const float* d_queries, int64_t nq,
                         int32_t topk, int32_t ef_search, int32_t* d_nns, float* d_distances,
                         int32_t* d_found_cnt, void* stream);
+
+/*
+ * Partitioned records across processes (one process per GPU). gann_part_export
+ * writes, into `blob` (GANN_PART_BLOB_BYTES), CUDA IPC handles of the handle's
+ * own record range; another process passes that blob to gann_part_attach with
+ * the range's index, which maps the range into its address space (peer access
+ * over NVLink is enabled on first use). Search returns GANN_ESTATE until every
+ * range is present. Attached ranges are unmapped by gann_close. Blobs are
+ * opaque and valid while the exporting handle is open.
+ */
+#define GANN_PART_BLOB_BYTES 512
+int gann_part_export(gann_handle* h, void* blob, int64_t blob_bytes);
+int gann_part_attach(gann_handle* h, int32_t part, const void* blob, int64_t blob_bytes);
 
 /* Release device and host memory of the handle (GustANN::~GustANN,
  * src/ssd_search.cu:112-137). NULL is accepted. */

@@ -42,6 +42,8 @@ INDEXES = {
     "f32": (datagen.MixtureSpec("deep", 12000, 96, 60, 0.1, center_scale=0.15), 64, 32, 1500, True),
     "f32_odd": (datagen.MixtureSpec("deep", 4000, 40, 20, 0.1, center_scale=0.15), 96, 12, 500, True),
     "u8_nonav": (datagen.MixtureSpec("sift", 6000, 64, 30, 20.0), 48, 16, 0, False),
+    # configuration-4 shape: 768 dims, 96 PQ chunks of 8 dims (per-query tables)
+    "f32_wide": (datagen.MixtureSpec("deep", 3000, 768, 20, 0.1, center_scale=0.15), 64, 96, 400, True),
 }
 
 

@@ -1,9 +1,10 @@
 """TEST INFRASTRUCTURE: a host-side model of the CUDA traversal's pool mechanics.
 
 `kernel_expansions` mirrors `traverse()` in gustann_b200/csrc/gann_search.cu
-step for step at warp-chunk granularity -- 64-bit candidate keys, the lossy
-pool-membership table and its hash, the per-query visited-id table (every
-evaluated id, never cleared within a query), the "beyond the last entry" and
+step for step at warp-chunk granularity -- 64-bit candidate keys, the
+per-query visited-id table and its hash (every evaluated id, never cleared
+within a query; absent when the search has no table buffer), optionally a
+pool-membership table (an id only while it is in the pool), the "beyond the last entry" and
 duplicate drops, ranks by lower bound, the next node chosen before the merge,
 the shifts from sorted survivor ranks + high-to-low moves starting at the
 smallest survivor rank's chunk, and the first-unvisited lower bound -- so that
@@ -101,7 +102,7 @@ def reference_expansions(entry, neighbours, adc, L, max_hops=1 << 14):
     return out, False
 
 
-def kernel_expansions(entry, neighbours, adc, L, max_hops=1 << 14, vis_bits=11):
+def kernel_expansions(entry, neighbours, adc, L, max_hops=1 << 14, vis_bits=11, pool_filter=False):
     """Model of the CUDA traverse(); returns the expanded ids. `vis_bits`
     None models a search without the visited-id table."""
     pl = (L + WARP - 1) // WARP
@@ -124,7 +125,7 @@ def kernel_expansions(entry, neighbours, adc, L, max_hops=1 << 14, vis_bits=11):
     for _ in range(max_hops):
         out.append(u)
         nb = list(neighbours(u))
-        ok = [filt[fslot(v)] != v and (vis is None or vis[vslot(v)] != v) for v in nb]
+        ok = [(not pool_filter or filt[fslot(v)] != v) and (vis is None or vis[vslot(v)] != v) for v in nb]
         ev = [v for v, k in zip(nb, ok) if k]
         dsum = dict(zip(ev, adc(ev).tolist())) if ev else {}
         if vis is not None:

@@ -171,3 +171,35 @@ def test_cli_usage_and_errors():
     r = subprocess.run([cli, "--query", "x", "--index", "/nonexistent", "--pq_data", "p", "--data_type", "uint8",
                         "--ef_search", "10", "--topk", "10"], capture_output=True, text=True)
     assert r.returncode != 0 and "cannot open index file" in r.stderr
+
+
+def test_config_struct_matches_the_header(tmp_path):
+    """ctypes' gann_config has the C struct's size and field offsets."""
+    import ctypes
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "gann.h"\n'
+                   'int main(void){printf("%zu %zu %zu %zu\\n", sizeof(gann_config), offsetof(gann_config, layout),'
+                   ' offsetof(gann_config, part_count), offsetof(gann_config, part_index)); return 0;}\n')
+    exe = tmp_path / "sz"
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    C = api._Config
+    assert got == [ctypes.sizeof(C), C.layout.offset, C.part_count.offset, C.part_index.offset]
+
+
+def test_split_record_options_are_validated(tmp_path):
+    p = _copy_golden(tmp_path)
+    cfg = GustANNConfig(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"])
+    for count, index, gpu_mem, code in [(9, 0, True, api.GANN_EINVAL), (-1, 0, True, api.GANN_EINVAL),
+                                        (2, 2, True, api.GANN_EINVAL), (3, -2, True, api.GANN_EINVAL),
+                                        (2, 0, False, api.GANN_EUNSUPPORTED)]:
+        g = GustANN(formats.UINT8)
+        with pytest.raises(GustANNError) as e:
+            g.init_pure_mem(cfg, gpu_mem, part_count=count, part_index=index)
+        assert e.value.code == code, (count, index, gpu_mem, str(e.value))
+
+
+def test_part_calls_reject_bad_arguments():
+    blob = b"\0" * api.PART_BLOB_BYTES
+    assert api.lib.gann_part_export(None, None, 0) == api.GANN_EINVAL
+    assert api.lib.gann_part_attach(None, 0, blob, len(blob)) == api.GANN_EINVAL

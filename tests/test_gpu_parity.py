@@ -173,8 +173,15 @@ def test_bad_arguments_raise(handles):
         g.query(q, 10, 100000)      # ef beyond the supported maximum
 
 
+# The reference's own kernels did not finish on the 768-dim, 96-chunk index
+# (f32_wide) within the 25 minutes of a test run on a B200, so they are not
+# run on that shape again; its parity rests on the oracle, which the
+# reference's kernels pin on the other shapes.
+REF_SHAPES = [n for n in INDEXES if n != "f32_wide"]
+
+
 @pytest.mark.skipif(not RefGPU.available(), reason="reference library not built")
-@pytest.mark.parametrize("name", list(INDEXES))
+@pytest.mark.parametrize("name", REF_SHAPES)
 def test_reference_kernels_agree(handles, name):
     """The reference's own compiled kernels on the B200, same files and queries.
 

@@ -26,8 +26,8 @@ def _load(name):
 
 @pytest.mark.parametrize("name", list(GOLD))
 @pytest.mark.parametrize("ef", [10, 33, 64, 200])
-@pytest.mark.parametrize("vis_bits", [None, 5, 11])
-def test_kernel_mechanics_equal_reference_merge(name, ef, vis_bits):
+@pytest.mark.parametrize("vis_bits,pool_filter", [(None, False), (5, False), (11, False), (None, True), (5, True)])
+def test_kernel_mechanics_equal_reference_merge(name, ef, vis_bits, pool_filter):
     o, deg, nbrs, codes, q = _load(name)
     luts = o.lut(q[:24])
     _, entries, _ = o.nav(q[:24])
@@ -42,7 +42,7 @@ def test_kernel_mechanics_equal_reference_merge(name, ef, vis_bits):
             return adc_sums(lut, codes, ids)
 
         ref, stale = reference_expansions(int(entries[t]), neighbours, adc, ef)
-        ker = kernel_expansions(int(entries[t]), neighbours, adc, ef, vis_bits=vis_bits)
+        ker = kernel_expansions(int(entries[t]), neighbours, adc, ef, vis_bits=vis_bits, pool_filter=pool_filter)
         assert ker == ref, f"query {t}: expansions differ"
         assert len(ref) == hops[t]
         assert stale == bool(flags[t] & 2)

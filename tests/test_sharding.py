@@ -91,3 +91,42 @@ def test_failed_rank_is_reported(tmp_path):
     assert (tmp_path / "err1.txt").read_text() == "injected rank failure"
     assert (tmp_path / "err0.txt").exists()
     assert not (tmp_path / "res.npz").exists()
+
+
+class _FakePartHandle:
+    """Stands in for a GustANN handle: records what it exported and attached."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.attached = {}
+
+    def export_part(self):
+        return f"range-{self.rank}".encode()
+
+    def attach_part(self, part, blob):
+        assert part not in self.attached and part != self.rank
+        self.attached[part] = blob
+
+
+def _exchange_worker(rank, world, port, out_dir):
+    import datetime
+    import torch.distributed as dist
+    from gustann_b200.sharding import exchange_parts
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        h = _FakePartHandle(rank)
+        exchange_parts(h, rank, world)
+        with open(os.path.join(out_dir, f"{rank}.txt"), "w") as f:
+            f.write(";".join(f"{k}={v.decode()}" for k, v in sorted(h.attached.items())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_exchange_parts_gives_every_rank_every_other_range(tmp_path, world):
+    mp.spawn(_exchange_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        got = open(tmp_path / f"{r}.txt").read()
+        want = ";".join(f"{k}=range-{k}" for k in range(world) if k != r)
+        assert got == want
