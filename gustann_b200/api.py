@@ -28,7 +28,8 @@ STATUS_NAMES = ["OK", "EINVAL", "EIO", "ENOMEM", "ECUDA", "ETIMEDOUT", "EUNSUPPO
 # Every symbol include/gann.h declares.
 EXPORTS = ["gann_open", "gann_open_device", "gann_search", "gann_search_device", "gann_close", "gann_last_error",
            "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample", "gann_set_option",
-           "gann_search_noalloc", "gann_part_export", "gann_part_attach"]
+           "gann_search_noalloc", "gann_part_export", "gann_part_attach", "gann_hop_begin", "gann_hop_requests",
+           "gann_hop_step", "gann_hop_finish", "gann_hop_free", "gann_read_pages"]
 GANN_OPT_ADC_MODE, GANN_OPT_PIVOT_WARPS, GANN_OPT_NEIGHBOUR_CODES = 1, 2, 3
 LAYOUT_AUTO, LAYOUT_SEPARATE, LAYOUT_NEIGHBOUR_CODES = 0, 1, 2
 ADC_AUTO, ADC_TABLE, ADC_PIVOT = 0, 1, 2
@@ -88,6 +89,12 @@ def _load() -> C.CDLL:
     lib.gann_search_noalloc.argtypes = [C.POINTER(_DeviceIndex), vp, i64, i32, i32, vp, vp, vp, vp]
     lib.gann_part_export.argtypes = [vp, vp, i64]
     lib.gann_part_attach.argtypes = [vp, i32, C.c_char_p, i64]
+    lib.gann_hop_begin.argtypes = [vp, fp, i64, i32, i32, C.POINTER(vp)]
+    lib.gann_hop_requests.argtypes = [vp, ip, C.POINTER(i64)]
+    lib.gann_hop_step.argtypes = [vp, vp]
+    lib.gann_hop_finish.argtypes = [vp, ip, fp, ip]
+    lib.gann_hop_free.argtypes = [vp]
+    lib.gann_read_pages.argtypes = [C.c_char_p, ip, i64, i32, vp, i32]
     for name in EXPORTS:
         if name != "gann_last_error":
             getattr(lib, name).restype = C.c_int
@@ -197,6 +204,23 @@ class GustANN:
                            (found_cnt, np.int32, num_queries)):
             if arr.dtype != dt or not arr.flags.c_contiguous or arr.size < n:
                 raise GustANNError(GANN_EINVAL, "search: output arrays must be contiguous int32/float32 of the right size")
+        if getattr(self, "_hybrid", None) is not None:
+            import time
+            t0 = time.perf_counter()
+            batch = self._hybrid[0] or max(num_queries, 1)
+            rounds = 0
+            for lo in range(0, num_queries, batch):
+                hi = min(num_queries, lo + batch)
+                n_, d_, f_, r_ = self.hop_search(q.reshape(-1, self.dim)[lo:hi], topk, ef_search,
+                                                 threads=self._hybrid[1])
+                nns.reshape(-1, topk)[lo:hi] = n_
+                distances.reshape(-1, topk)[lo:hi] = d_
+                found_cnt.reshape(-1)[lo:hi] = f_
+                rounds += r_
+            if stats is not None:
+                stats.run_time = stats.total_time = time.perf_counter() - t0
+                stats.hops = rounds
+            return
         st = _Stats()
         _check(lib.gann_search(self._h, _ptr(q), num_queries, topk, ef_search, _ptr(nns), _ptr(distances),
                                _ptr(found_cnt), C.byref(st)))
@@ -239,6 +263,57 @@ class GustANN:
         _check(lib.gann_probe_entry(self._h, _ptr(q), q.shape[0], _ptr(s), _ptr(e)))
         return s, e
 
+    def init_hybrid(self, config: GustANNConfig, hybrid_config=None) -> None:
+        """``GustANN::init_hybrid`` (``src/ssd_search.cu:81-106``): node records
+        stay in the index file; :meth:`search` and :meth:`query` then run the
+        host-driven hop search (:meth:`hop_search`). ``hybrid_config`` may carry
+        ``mini_batch`` and ``thread_cnt`` (``HybridExecutorConfig``)."""
+        self.close()
+        cfg = _Config(config.index_file.encode(), config.pq_file_prefix.encode(),
+                      (config.nav_graph_prefix or "").encode(), self.data_type, 2, self.device, 1, 0, 0)
+        h = C.c_void_p()
+        _check(lib.gann_open(C.byref(cfg), C.byref(h)))
+        self._h = h
+        self.dim = self.info()["dim"]
+        self._index_file = config.index_file
+        self._hybrid = (getattr(hybrid_config, "mini_batch", 0) or 0, getattr(hybrid_config, "thread_cnt", 0) or 0)
+
+    def hop_search(self, queries: np.ndarray, topk: int, ef_search: int, index_file: str | None = None,
+                   threads: int = 0, read_pages=None):
+        """Host-driven search, one hop per round (``gann_hop_*``): between hops
+        the 4 KB page of every query's requested node is read from
+        ``index_file`` (``gann_read_pages``), or by ``read_pages(ids, pages)``
+        when given. Returns ``(nns, distances, found_cnt, rounds)``."""
+        self._need()
+        q = np.ascontiguousarray(queries, dtype=np.float32).reshape(-1, self.dim)
+        nq = q.shape[0]
+        index_file = index_file or getattr(self, "_index_file", None)
+        npp = self.info()["nodes_per_page"]
+        b = C.c_void_p()
+        _check(lib.gann_hop_begin(self._h, _ptr(q), nq, topk, ef_search, C.byref(b)))
+        try:
+            ids = np.full(nq, -1, np.int32)
+            pages = np.zeros((nq, 4096), np.uint8)
+            active = C.c_int64()
+            rounds = 0
+            while True:
+                _check(lib.gann_hop_requests(b, _ptr(ids), C.byref(active)))
+                if active.value == 0:
+                    break
+                if read_pages is not None:
+                    read_pages(ids, pages)
+                else:
+                    _check(lib.gann_read_pages(index_file.encode(), _ptr(ids), nq, npp, _ptr(pages), threads))
+                _check(lib.gann_hop_step(b, _ptr(pages)))
+                rounds += 1
+            nns = np.zeros((nq, topk), np.int32)
+            dist = np.zeros((nq, topk), np.float32)
+            found = np.zeros(nq, np.int32)
+            _check(lib.gann_hop_finish(b, _ptr(nns), _ptr(dist), _ptr(found)))
+        finally:
+            lib.gann_hop_free(b)
+        return nns, dist, found, rounds
+
     def export_part(self) -> bytes:
         """``gann_part_export``: an opaque blob naming this handle's record
         range for :meth:`attach_part` in another process."""
@@ -271,6 +346,7 @@ class GustANN:
         if self._h is not None:
             lib.gann_close(self._h)
             self._h = None
+        self._hybrid = None
 
     def _need(self) -> None:
         if self._h is None:

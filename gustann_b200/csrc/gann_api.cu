@@ -1,6 +1,10 @@
 // C ABI of libgann.so: index load onto one B200, search orchestration, stage
 // probes. See include/gann.h for the contract of every entry point.
 #include <algorithm>
+#include <unistd.h>
+#include <fcntl.h>
+#include <thread>
+#include <atomic>
 #include <chrono>
 #include <cstring>
 #include <memory>
@@ -48,6 +52,7 @@ struct gann_handle {
   int device = 0;
   int dtype = GANN_FLOAT;
   bool host_records = false;
+  bool storage_records = false;      // records left on storage (host-driven hops only)
   bool cuda_ready = false;           // a CUDA context exists for `device`
   bool owns_records = true;          // false: vectors/adjacency/codes belong to the caller
   HostIndex hi;
@@ -283,7 +288,9 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
     return set_error(GANN_EINVAL, "gann_open: dtype must be GANN_UINT8 or GANN_FLOAT");
   h->device = cfg->device;
   h->dtype = cfg->dtype;
+  if (cfg->use_gpu_mem < 0 || cfg->use_gpu_mem > 2) return set_error(GANN_EINVAL, "gann_open: use_gpu_mem must be 0, 1 or 2");
   h->host_records = cfg->use_gpu_mem == 0;
+  h->storage_records = cfg->use_gpu_mem == 2;
   if (cfg->layout < 0 || cfg->layout > 2) return set_error(GANN_EINVAL, "gann_open: layout must be 0, 1 or 2");
   if (cfg->part_count < 0 || cfg->part_count > gann::kMaxParts)
     return set_error(GANN_EINVAL, "gann_open: part_count must be 0..8");
@@ -291,7 +298,7 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
   h->part_index = h->part_count ? cfg->part_index : 0;
   if (h->part_count && (h->part_index < -1 || h->part_index >= h->part_count))
     return set_error(GANN_EINVAL, "gann_open: part_index must be -1..part_count-1");
-  if (h->part_count && h->host_records)
+  if (h->part_count && (h->host_records || h->storage_records))
     return set_error(GANN_EUNSUPPORTED, "gann_open: split records need use_gpu_mem = 1");
 
   // parse and validate every file before touching the GPU
@@ -356,6 +363,7 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
   GANN_CUDA(cudaMalloc(reinterpret_cast<void**>(&h->counter), 4 * sizeof(int32_t)));
   GANN_CUDA(alloc_vis(h));
   if (h->part_count) return load_parts(h, cfg);
+  if (h->storage_records) return GANN_OK;   // pages are read per hop by the caller
   if ((rc = load_records(h, cfg->index_file))) return rc;
   if (cfg->layout != 1) {
     // neighbour codes next to the adjacency: built on the GPU from the records
@@ -542,6 +550,176 @@ int gann_open(const gann_config* cfg, gann_handle** out) {
   return GANN_OK;
 }
 
+// ----------------------------------------------------------------- host-driven hops
+struct gann_hop_batch {
+  gann_handle* h = nullptr;
+  gann::HopState s;
+  float* d_q = nullptr;
+  uint8_t* d_pages = nullptr;
+  void release() {
+    if (!h) return;
+    cudaSetDevice(h->device);
+    for (void* p : {static_cast<void*>(s.qpp), static_cast<void*>(s.lut), static_cast<void*>(s.pool),
+                    static_cast<void*>(s.psize), static_cast<void*>(s.request), static_cast<void*>(s.nns),
+                    static_cast<void*>(s.dist), static_cast<void*>(s.found), static_cast<void*>(s.hops),
+                    static_cast<void*>(s.err), static_cast<void*>(d_q), static_cast<void*>(d_pages)})
+      if (p) cudaFree(p);
+    s = gann::HopState();
+    d_q = nullptr;
+    d_pages = nullptr;
+  }
+};
+
+}  // extern "C"
+
+namespace {
+template <typename T>
+cudaError_t dalloc(T*& p, int64_t count) {
+  return cudaMalloc(reinterpret_cast<void**>(&p), sizeof(T) * static_cast<size_t>(std::max<int64_t>(count, 1)));
+}
+
+int hop_begin_impl(gann_handle* h, const float* queries, int64_t nq, int32_t topk, int32_t ef, gann_hop_batch* b) {
+  const HostIndex& hi = h->hi;
+  gann::HopState& s = b->s;
+  s.nq = nq;
+  s.topk = topk;
+  s.ef = ef;
+  s.max_hops = std::max(1 << 14, 64 * ef);
+  s.nav_max_hops = 1 << 20;
+  GANN_CUDA(cudaSetDevice(h->device));
+  GANN_CUDA(dalloc(s.qpp, nq * hi.dim));
+  GANN_CUDA(dalloc(s.lut, nq * hi.num_chunks * gann::kPivots));
+  GANN_CUDA(dalloc(s.pool, nq * ef));
+  GANN_CUDA(dalloc(s.psize, nq));
+  GANN_CUDA(dalloc(s.request, nq));
+  GANN_CUDA(dalloc(s.nns, nq * topk));
+  GANN_CUDA(dalloc(s.dist, nq * topk));
+  GANN_CUDA(dalloc(s.found, nq));
+  GANN_CUDA(dalloc(s.hops, nq));
+  GANN_CUDA(dalloc(s.err, 3));
+  GANN_CUDA(dalloc(b->d_q, nq * hi.dim));
+  GANN_CUDA(dalloc(b->d_pages, nq * gann::kPageSize));
+  GANN_CUDA(cudaMemsetAsync(s.err, 0, 3 * sizeof(int32_t), h->stream));
+  if (nq > 0)
+    GANN_CUDA(cudaMemcpyAsync(b->d_q, queries, sizeof(float) * nq * hi.dim, cudaMemcpyHostToDevice, h->stream));
+  GANN_CUDA(gann::launch_hop_begin(h->ix, b->d_q, s, h->dtype, h->stream));
+  GANN_CUDA(cudaStreamSynchronize(h->stream));
+  return GANN_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int gann_hop_begin(gann_handle* h, const float* queries, int64_t nq, int32_t topk, int32_t ef_search,
+                   gann_hop_batch** out) {
+  if (!out) return set_error(GANN_EINVAL, "gann_hop_begin: null output");
+  *out = nullptr;
+  int rc = check_search_args(h, nq, topk, ef_search);
+  if (rc) return rc;
+  if (nq > 0 && !queries) return set_error(GANN_EINVAL, "gann_hop_begin: null queries");
+  if (h->part_count) return set_error(GANN_EUNSUPPORTED, "gann_hop_begin: not with split records");
+  if ((h->hi.dim * h->hi.elem) % 4 != 0 || h->hi.max_node_len % 4 != 0)
+    return set_error(GANN_EUNSUPPORTED, "gann_hop_begin: records must be 4-byte aligned within a page");
+  auto* b = new (std::nothrow) gann_hop_batch;
+  if (!b) return set_error(GANN_ENOMEM, "gann_hop_begin: out of host memory");
+  b->h = h;
+  rc = hop_begin_impl(h, queries, nq, topk, ef_search, b);
+  if (rc) {
+    b->release();
+    delete b;
+    return rc;
+  }
+  *out = b;
+  return GANN_OK;
+}
+
+int gann_hop_requests(gann_hop_batch* b, int32_t* node_ids, int64_t* active) {
+  if (!b || !b->h || (b->s.nq > 0 && !node_ids)) return set_error(GANN_EINVAL, "gann_hop_requests: bad argument");
+  gann_handle* h = b->h;
+  GANN_CUDA(cudaSetDevice(h->device));
+  if (b->s.nq > 0) {
+    GANN_CUDA(cudaMemcpyAsync(node_ids, b->s.request, sizeof(int32_t) * b->s.nq, cudaMemcpyDeviceToHost, h->stream));
+    GANN_CUDA(cudaStreamSynchronize(h->stream));
+  }
+  int64_t n = 0;
+  for (int64_t i = 0; i < b->s.nq; ++i) n += node_ids[i] >= 0;
+  if (active) *active = n;
+  return GANN_OK;
+}
+
+int gann_hop_step(gann_hop_batch* b, const void* pages) {
+  if (!b || !b->h || (b->s.nq > 0 && !pages)) return set_error(GANN_EINVAL, "gann_hop_step: bad argument");
+  gann_handle* h = b->h;
+  GANN_CUDA(cudaSetDevice(h->device));
+  if (b->s.nq == 0) return GANN_OK;
+  GANN_CUDA(cudaMemcpyAsync(b->d_pages, pages, static_cast<size_t>(b->s.nq) * gann::kPageSize,
+                            cudaMemcpyHostToDevice, h->stream));
+  GANN_CUDA(gann::launch_hop_step(h->ix, b->s, b->d_pages, static_cast<int32_t>(h->hi.max_node_len),
+                                  static_cast<int32_t>(h->hi.nodes_per_page), h->dtype, h->stream));
+  GANN_CUDA(cudaStreamSynchronize(h->stream));
+  return GANN_OK;
+}
+
+int gann_hop_finish(gann_hop_batch* b, int32_t* nns, float* distances, int32_t* found_cnt) {
+  if (!b || !b->h || (b->s.nq > 0 && (!nns || !distances || !found_cnt)))
+    return set_error(GANN_EINVAL, "gann_hop_finish: bad argument");
+  gann_handle* h = b->h;
+  const gann::HopState& s = b->s;
+  GANN_CUDA(cudaSetDevice(h->device));
+  if (s.nq > 0) {
+    GANN_CUDA(cudaMemcpyAsync(nns, s.nns, sizeof(int32_t) * s.nq * s.topk, cudaMemcpyDeviceToHost, h->stream));
+    GANN_CUDA(cudaMemcpyAsync(distances, s.dist, sizeof(float) * s.nq * s.topk, cudaMemcpyDeviceToHost, h->stream));
+    GANN_CUDA(cudaMemcpyAsync(found_cnt, s.found, sizeof(int32_t) * s.nq, cudaMemcpyDeviceToHost, h->stream));
+  }
+  int32_t errs[3] = {0, 0, 0};
+  GANN_CUDA(cudaMemcpyAsync(errs, s.err, sizeof(errs), cudaMemcpyDeviceToHost, h->stream));
+  GANN_CUDA(cudaStreamSynchronize(h->stream));
+  if (errs[2]) return set_error(GANN_EINVAL, "gann_hop_finish: " + std::to_string(errs[2]) +
+                                                 " page(s) held records that are not this index's");
+  return GANN_OK;
+}
+
+int gann_read_pages(const char* index_file, const int32_t* node_ids, int64_t n, int32_t nodes_per_page,
+                    void* pages, int32_t threads) {
+  if (!index_file || n < 0 || nodes_per_page <= 0 || (n > 0 && (!node_ids || !pages)))
+    return set_error(GANN_EINVAL, "gann_read_pages: bad argument");
+  const int fd = ::open(index_file, O_RDONLY);
+  if (fd < 0) return set_error(GANN_EIO, std::string("gann_read_pages: cannot open ") + index_file);
+  int nt = threads > 0 ? threads : static_cast<int>(std::thread::hardware_concurrency());
+  nt = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({static_cast<int64_t>(nt), int64_t(64), n})));
+  std::atomic<int64_t> bad{-1};
+  auto work = [&](int t) {
+    for (int64_t i = t; i < n; i += nt) {
+      const int32_t id = node_ids[i];
+      if (id < 0) continue;
+      const off_t off = static_cast<off_t>(gann::kPageSize) * (1 + id / nodes_per_page);
+      uint8_t* dst = static_cast<uint8_t*>(pages) + i * gann::kPageSize;
+      ssize_t got = 0;
+      while (got < gann::kPageSize) {
+        const ssize_t r = ::pread(fd, dst + got, gann::kPageSize - got, off + got);
+        if (r <= 0) break;
+        got += r;
+      }
+      if (got != gann::kPageSize) bad.store(i);
+    }
+  };
+  std::vector<std::thread> pool;
+  for (int t = 1; t < nt; ++t) pool.emplace_back(work, t);
+  work(0);
+  for (auto& th : pool) th.join();
+  ::close(fd);
+  if (bad.load() >= 0)
+    return set_error(GANN_EIO, "gann_read_pages: short read for node " + std::to_string(node_ids[bad.load()]));
+  return GANN_OK;
+}
+
+int gann_hop_free(gann_hop_batch* b) {
+  if (!b) return GANN_OK;
+  b->release();
+  delete b;
+  return GANN_OK;
+}
+
 int gann_close(gann_handle* h) {
   if (!h) return GANN_OK;
   h->release();
@@ -643,8 +821,8 @@ int gann_set_option(gann_handle* h, int32_t option, int64_t value) {
       h->ix.adc_mode = static_cast<int32_t>(value);
       return GANN_OK;
     case GANN_OPT_PIVOT_WARPS:
-      if (value != 0 && (value < 8 || value > 20))
-        return set_error(GANN_EINVAL, "gann_set_option: pivot warps must be 0 or 8..20");
+      if (value != 0 && (value < 8 || value > 24))
+        return set_error(GANN_EINVAL, "gann_set_option: pivot warps must be 0 or 8..24");
       h->ix.piv_warps = static_cast<int32_t>(value);
       return GANN_OK;
     case GANN_OPT_NEIGHBOUR_CODES:
@@ -680,6 +858,7 @@ int gann_search_device(gann_handle* h, const float* d_queries, int64_t nq, int32
                        void* stream) {
   int rc = check_search_args(h, nq, topk, ef_search);
   if (rc) return rc;
+  if (h->storage_records) return set_error(GANN_ESTATE, "search: records are on storage; use gann_hop_*");
   if (nq == 0) return GANN_OK;
   if (!d_queries || !d_nns || !d_distances || !d_found_cnt)
     return set_error(GANN_EINVAL, "gann_search_device: null buffer");
@@ -697,6 +876,7 @@ int gann_search(gann_handle* h, const float* queries, int64_t nq, int32_t topk, 
   const auto t0 = std::chrono::steady_clock::now();
   int rc = check_search_args(h, nq, topk, ef_search);
   if (rc) return rc;
+  if (h->storage_records) return set_error(GANN_ESTATE, "search: records are on storage; use gann_hop_*");
   if (stats) std::memset(stats, 0, sizeof(*stats));
   if (nq == 0) return GANN_OK;
   if (!queries || !nns || !distances || !found_cnt) return set_error(GANN_EINVAL, "gann_search: null buffer");

@@ -72,7 +72,7 @@ struct DeviceIndex {
   // each code_stride bytes (nullptr when the index keeps codes separate only)
   const uint8_t* ncodes = nullptr;
   int32_t adc_mode = 0;     // 0 auto, 1 table, 2 pivot
-  int32_t piv_warps = 0;    // 0 = as many as fit (<= 20)
+  int32_t piv_warps = 0;    // 0 = as many as fit (<= 24)
   // records split by id (nparts > 1): part p holds ids [p << part_shift,
   // (p + 1) << part_shift) in its own arrays (possibly another GPU's memory,
   // reached through peer pointers); vecs/adj/ncodes above are then unused
@@ -107,7 +107,30 @@ struct SearchArgs {
 constexpr int kVisBits = 11;
 constexpr int kVisWarpsPerSM = 32;
 
+// Host-driven search, one hop per call: the reference's SSD-hybrid mode
+// (src/hyd_task_runner.cu, src/impl/hyd_search_v2.cuh), in which the caller
+// fetches the 4 KB page of every query's next node between hops. Per-query
+// state lives in device memory between calls.
+struct HopState {
+  int64_t nq = 0;
+  int32_t topk = 0, ef = 0, max_hops = 0, nav_max_hops = 0;
+  float* qpp = nullptr;       // [nq x dim] q'' = (q - c) + c
+  float* lut = nullptr;       // [nq x M x 256] ADC tables
+  uint64_t* pool = nullptr;   // [nq x ef] keys (see gann_search.cu)
+  int32_t* psize = nullptr;   // [nq]
+  int32_t* request = nullptr; // [nq] node expanded next, -1 when done
+  int32_t* nns = nullptr;     // [nq x topk]
+  float* dist = nullptr;      // [nq x topk]
+  int32_t* found = nullptr;   // [nq]
+  uint32_t* hops = nullptr;   // [nq]
+  int32_t* err = nullptr;     // [3]: capped queries, capped nav searches, bad records
+};
+
 // Kernel launchers (gann_search.cu)
+cudaError_t launch_hop_begin(const DeviceIndex& ix, const float* d_q, const HopState& s, int dtype,
+                             cudaStream_t st);
+cudaError_t launch_hop_step(const DeviceIndex& ix, const HopState& s, const uint8_t* d_pages, int32_t node_len,
+                            int32_t nodes_per_page, int dtype, cudaStream_t st);
 cudaError_t launch_search(const DeviceIndex& ix, const SearchArgs& a, int dtype,
                           int sm_count, cudaStream_t st);
 cudaError_t launch_probe_lut(const DeviceIndex& ix, const float* d_q, int64_t nq,

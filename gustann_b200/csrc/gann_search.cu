@@ -798,12 +798,14 @@ __global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, con
 }
 
 // Pivot mode: one persistent CTA per SM holds the 256 x D pivot table once
-// (M x 3 KB for 3-dim chunks, M x 4 KB otherwise) and runs up to kPivWarps
+// (M x 3 KB for 3-dim chunks, M x 4 KB otherwise) and runs up to piv_warps_max
 // queries at a time, one per warp, each with a few KB of private state instead
 // of a 4*M KB table.
-constexpr int kPivWarps = 20;
+// Queries per SM: 24 at two neighbours per lane (80 registers a thread, no
+// spills); 20 at four, whose extra registers would spill at 24.
+constexpr int piv_warps_max(int npl) { return npl > 2 ? 20 : 24; }
 template <typename T, int NPL, int VP, int CW>
-__global__ void __launch_bounds__(kWarp * kPivWarps, 1) search_kernel_piv(const DeviceIndex ix, const SearchArgs a,
+__global__ void __launch_bounds__(kWarp * piv_warps_max(NPL), 1) search_kernel_piv(const DeviceIndex ix, const SearchArgs a,
                                                                           size_t per_warp, int pl) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int ntab = ix.chunks * kPivots;
@@ -882,7 +884,7 @@ cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_co
     const size_t tab = piv_tab_bytes(ix.piv_width, ix.chunks);
     const size_t per_warp = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, true);
     int warps = tab < static_cast<size_t>(optin)
-                    ? static_cast<int>(std::min<size_t>(kPivWarps, (optin - tab) / per_warp)) : 0;
+                    ? static_cast<int>(std::min<size_t>(piv_warps_max(NPL), (optin - tab) / per_warp)) : 0;
     if (ix.piv_warps > 0) warps = std::min(warps, ix.piv_warps);
     if (warps >= 8) {
       const size_t smem = tab + per_warp * warps;
@@ -922,12 +924,223 @@ cudaError_t launch_typed(const DeviceIndex& ix, const SearchArgs& a, int sm_coun
   return launch_vp<T, 32>(ix, a, sm_count, st);
 }
 
+// ---------------------------------------------------------------------------
+// Host-driven search, one hop per launch (the reference's SSD-hybrid mode:
+// init_search + get_entry_kernel_inner, then per hop merge_data_kernel +
+// unify_kernel; src/hyd_task_runner.cu:12-15,55-66,126-178,
+// src/impl/hyd_search_v2.cuh:8-472). The caller supplies, per query, the 4 KB
+// page holding the record of the node the previous step asked for. As in the
+// reference's hybrid mode, the pivot-graph entry is searched with q'' (the
+// query after init_query's in-place q -= c ... q += c), and so is the re-rank.
+// Not a throughput path: the state of every query lives in device memory
+// between launches, one warp works on one query.
+
+// Query setup: q'' and the ADC table of each query, its entry node, empty
+// pool and top-k.
+template <typename T>
+__global__ void __launch_bounds__(128) hop_begin_kernel(const DeviceIndex ix, const float* __restrict__ q,
+                                                        const HopState s) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp, wpb = blockDim.x / kWarp;
+  const int dpad = (ix.dim + 3) & ~3;
+  float* qc = reinterpret_cast<float*>(smem) + static_cast<size_t>(warp) * 2 * dpad;
+  float* qs = qc + dpad;
+  for (int64_t qid = static_cast<int64_t>(blockIdx.x) * wpb + warp; qid < s.nq;
+       qid += static_cast<int64_t>(gridDim.x) * wpb) {
+    const float* qq = q + qid * ix.dim;
+    float* qpp = s.qpp + qid * ix.dim;
+    for (int i = lane; i < ix.dim; i += kWarp) {
+      const float c = __ldg(ix.centroid + i);
+      const float d = __fsub_rn(qq[i], c);
+      const float r = __fadd_rn(d, c);
+      qc[i] = d;
+      qs[i] = r;
+      qpp[i] = r;
+    }
+    __syncwarp();
+    build_lut(ix, qc, s.lut + qid * ix.chunks * kPivots, lane);
+    uint32_t entry = static_cast<uint32_t>(ix.medoid);
+    if (ix.has_nav) {
+      bool capped = false;
+      const int si = nav_search<T>(ix, qs, lane, s.nav_max_hops, capped);
+      const bool bad = si < 0 || si >= ix.nav_points;
+      if (!bad) entry = static_cast<uint32_t>(__ldg(ix.nav_map + si));
+      if ((capped || bad) && lane == 0) atomicAdd(s.err + 1, 1);
+    }
+    if (lane == 0) {
+      s.request[qid] = static_cast<int32_t>(entry);
+      s.psize[qid] = 0;
+      s.found[qid] = 0;
+      s.hops[qid] = 0;
+    }
+    for (int t = lane; t < s.topk; t += kWarp) {
+      s.nns[qid * s.topk + t] = 0;
+      s.dist[qid * s.topk + t] = 0.f;
+    }
+    __syncwarp();
+  }
+}
+
+// One hop of every query that has a request: exact distance of the requested
+// node u (re-rank), ADC of its neighbours, merge into the pool (first `ef`
+// distinct entries of merge(pool, sorted neighbours), pool copy first), and
+// the next request = the first unvisited pool entry (-1: the query is done).
+// Neighbour ids past the index, or a degree past the slots, count as bad
+// records (err[2]) and are dropped.
+template <typename T>
+__global__ void __launch_bounds__(128) hop_step_kernel(const DeviceIndex ix, const HopState s,
+                                                       const uint8_t* __restrict__ pages, int node_len, int npp) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp, wpb = blockDim.x / kWarp;
+  const int R = ix.degree, L = s.ef, M = ix.chunks;
+  uint64_t* nk = reinterpret_cast<uint64_t*>(smem) + static_cast<size_t>(warp) * (2 * R + L);
+  uint64_t* mg = nk + R;
+  for (int64_t qid = static_cast<int64_t>(blockIdx.x) * wpb + warp; qid < s.nq;
+       qid += static_cast<int64_t>(gridDim.x) * wpb) {
+    const int32_t u = s.request[qid];
+    if (u < 0) continue;
+    const uint32_t h = s.hops[qid] + 1;
+    if (h > static_cast<uint32_t>(s.max_hops)) {
+      if (lane == 0) {
+        s.request[qid] = -1;
+        atomicAdd(s.err, 1);
+      }
+      continue;
+    }
+    const uint8_t* rec = pages + qid * kPageSize + static_cast<size_t>(u % npp) * node_len;
+    const T* vec = reinterpret_cast<const T*>(rec);
+    const uint32_t* nbr = reinterpret_cast<const uint32_t*>(rec + static_cast<size_t>(ix.dim) * sizeof(T));
+    int deg = static_cast<int>(nbr[0]);
+    if (deg < 0 || deg > R) {
+      if (lane == 0) atomicAdd(s.err + 2, 1);
+      deg = deg < 0 ? 0 : R;
+    }
+    // re-rank u on q'' and insert after every equal top-k entry (retset_push_32)
+    const float ex = warp_sqdist<T>(s.qpp + qid * ix.dim, vec, ix.dim, lane);
+    if (lane == 0) {
+      const int cnt = s.found[qid];
+      int32_t* nn = s.nns + qid * s.topk;
+      float* dd = s.dist + qid * s.topk;
+      int le = 0;
+      while (le < cnt && dd[le] <= ex) ++le;
+      if (le < s.topk) {
+        for (int t = min(cnt, s.topk - 1); t > le; --t) {
+          dd[t] = dd[t - 1];
+          nn[t] = nn[t - 1];
+        }
+        dd[le] = ex;
+        nn[le] = u;
+      }
+      s.found[qid] = min(cnt + 1, s.topk);
+    }
+    // ADC of the neighbours, chunks in order
+    const float* lut = s.lut + qid * M * kPivots;
+    for (int e = lane; e < deg; e += kWarp) {
+      const uint32_t v = nbr[1 + e];
+      if (v >= static_cast<uint64_t>(ix.n)) {
+        atomicAdd(s.err + 2, 1);
+        nk[e] = ~0ull;
+        continue;
+      }
+      const uint8_t* code = ix.codes + static_cast<size_t>(v) * ix.code_stride;
+      float d = 0.f;
+      for (int j = 0; j < M; ++j) d = __fadd_rn(d, lut[j * kPivots + code[j]]);
+      nk[e] = make_key(d, v);
+    }
+    __syncwarp();
+    // a neighbour equal to a pool entry is dropped (the pool copy is kept)
+    const int ps = s.psize[qid];
+    uint64_t* pool = s.pool + qid * L;
+    for (int e = lane; e < deg; e += kWarp) {
+      if (nk[e] == ~0ull) continue;
+      const uint64_t kk = nk[e] >> 1;
+      int lo = 0, hi = ps;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if ((pool[mid] >> 1) < kk) lo = mid + 1; else hi = mid;
+      }
+      if (lo < ps && (pool[lo] >> 1) == kk) nk[e] = ~0ull;
+    }
+    __syncwarp();
+    int nsv = 0;
+    for (int e0 = 0; e0 < deg; e0 += kWarp) nsv += __popc(__ballot_sync(kFull, e0 + lane < deg && nk[e0 + lane] != ~0ull));
+    // merged positions: pool entry i -> i + #survivors below it; survivor e ->
+    // #survivors below it (ties by slot) + #pool entries below it
+    for (int i = lane; i < ps; i += kWarp) {
+      const uint64_t kk = pool[i] >> 1;
+      int below = 0;
+      for (int f = 0; f < deg; ++f) below += nk[f] != ~0ull && (nk[f] >> 1) < kk;
+      if (i + below < L) mg[i + below] = pool[i];
+    }
+    for (int e = lane; e < deg; e += kWarp) {
+      if (nk[e] == ~0ull) continue;
+      const uint64_t kk = nk[e] >> 1;
+      int below = 0;
+      for (int f = 0; f < deg; ++f)
+        below += nk[f] != ~0ull && ((nk[f] >> 1) < kk || ((nk[f] >> 1) == kk && f < e));
+      int lo = 0, hi = ps;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if ((pool[mid] >> 1) < kk) lo = mid + 1; else hi = mid;
+      }
+      if (below + lo < L) mg[below + lo] = nk[e];
+    }
+    __syncwarp();
+    const int nsz = min(ps + nsv, L);
+    // next request: the first unvisited entry
+    int first = -1;
+    for (int j0 = 0; j0 < nsz; j0 += kWarp) {
+      const unsigned bm = __ballot_sync(kFull, j0 + lane < nsz && (mg[j0 + lane] & 1ull));
+      if (bm) {
+        first = j0 + __ffs(bm) - 1;
+        break;
+      }
+    }
+    for (int j = lane; j < nsz; j += kWarp) pool[j] = j == first ? (mg[j] & ~1ull) : mg[j];
+    if (lane == 0) {
+      s.psize[qid] = nsz;
+      s.hops[qid] = h;
+      s.request[qid] = first >= 0 ? static_cast<int32_t>(static_cast<uint32_t>(mg[first]) >> 1) : -1;
+    }
+    __syncwarp();
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_gather_neighbour_codes(const uint32_t* adj, int adj_stride, int degree, const uint8_t* codes,
                                           int code_stride, int64_t n, uint8_t* out, cudaStream_t st) {
   gather_neighbour_codes<<<148 * 8, 256, 0, st>>>(adj, adj_stride, degree, reinterpret_cast<const uint4*>(codes),
                                                   code_stride / 16, n, reinterpret_cast<uint4*>(out));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_hop_begin(const DeviceIndex& ix, const float* d_q, const HopState& s, int dtype,
+                             cudaStream_t st) {
+  if (s.nq <= 0) return cudaSuccess;
+  const int wpb = 4;
+  const size_t smem = sizeof(float) * 2 * ((ix.dim + 3) & ~3) * wpb;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((s.nq + wpb - 1) / wpb, 148 * 16));
+  if (dtype == 0) hop_begin_kernel<uint8_t><<<grid, kWarp * wpb, smem, st>>>(ix, d_q, s);
+  else hop_begin_kernel<float><<<grid, kWarp * wpb, smem, st>>>(ix, d_q, s);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_hop_step(const DeviceIndex& ix, const HopState& s, const uint8_t* d_pages, int32_t node_len,
+                            int32_t nodes_per_page, int dtype, cudaStream_t st) {
+  if (s.nq <= 0) return cudaSuccess;
+  const int wpb = 4;
+  const size_t smem = sizeof(uint64_t) * (2 * static_cast<size_t>(ix.degree) + s.ef) * wpb;
+  if (smem > 48 * 1024) {
+    auto f8 = hop_step_kernel<uint8_t>;
+    auto f32 = hop_step_kernel<float>;
+    cudaError_t e = cudaFuncSetAttribute(dtype == 0 ? f8 : f32, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((s.nq + wpb - 1) / wpb, 148 * 16));
+  if (dtype == 0) hop_step_kernel<uint8_t><<<grid, kWarp * wpb, smem, st>>>(ix, s, d_pages, node_len, nodes_per_page);
+  else hop_step_kernel<float><<<grid, kWarp * wpb, smem, st>>>(ix, s, d_pages, node_len, nodes_per_page);
   return cudaGetLastError();
 }
 

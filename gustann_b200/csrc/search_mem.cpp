@@ -64,7 +64,10 @@ void usage() {
   std::fprintf(stderr,
                "usage: search_mem --query FILE --index FILE --pq_data PREFIX --data_type uint8|float\n"
                "                  [--nav_graph DIR] [--ground_truth FILE] [--topk K]\n"
-               "                  --ef_search L [L ...] [-R|--repeat N] [-G|--use-gpu-mem] [--device D]\n");
+               "                  --ef_search L [L ...] [-R|--repeat N] [-G|--use-gpu-mem] [--device D]\n"
+               "                  [--hybrid -B|--minibatch N -T|--thread N [--io_backend memory]]\n"
+               "  --hybrid: records stay in the index file and each hop reads the needed pages\n"
+               "            (the reference driver's HYBRID_CALC build, GustANN::init_hybrid)\n");
   std::exit(1);
 }
 
@@ -74,7 +77,8 @@ int main(int argc, char** argv) {
   std::string query_file, gt_file, data_type;
   gustann::GustANNConfig cfg;
   int topk = 100, repeat = 20, device = 0;
-  bool use_gpu_mem = false;
+  bool use_gpu_mem = false, hybrid = false;
+  gustann::HybridExecutorConfig hcfg;
   std::vector<int> efs;
   for (int i = 1; i < argc; ++i) {
     const std::string a = argv[i];
@@ -92,6 +96,16 @@ int main(int argc, char** argv) {
     else if (a == "--repeat" || a == "-R") repeat = std::atoi(need().c_str());
     else if (a == "--use-gpu-mem" || a == "-G") use_gpu_mem = true;
     else if (a == "--device") device = std::atoi(need().c_str());
+    else if (a == "--hybrid") hybrid = true;
+    else if (a == "--minibatch" || a == "-B") hcfg.mini_batch = std::atoi(need().c_str());
+    else if (a == "--thread" || a == "-T") hcfg.thread_cnt = std::atoi(need().c_str());
+    else if (a == "--ctx_per_thread" || a == "-C") hcfg.ctx_per_thread = std::atoi(need().c_str());
+    else if (a == "--io_backend") {
+      if (need() != "memory") {
+        std::fprintf(stderr, "only the 'memory' io_backend (pread of the index file) is available\n");
+        return 1;
+      }
+    }
     else if (a == "--ef_search") {
       while (i + 1 < argc && argv[i + 1][0] != '-') efs.push_back(std::atoi(argv[++i]));
     } else usage();
@@ -113,7 +127,8 @@ int main(int argc, char** argv) {
 
   gustann::GustANN a(dtype, device);
   try {
-    a.init_pure_mem(cfg, use_gpu_mem);
+    if (hybrid) a.init_hybrid(cfg, hcfg);
+    else a.init_pure_mem(cfg, use_gpu_mem);
   } catch (const std::exception& e) {
     std::fprintf(stderr, "%s\n", e.what());
     return 1;

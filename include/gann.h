@@ -49,7 +49,9 @@ typedef enum { GANN_UINT8 = 0, GANN_FLOAT = 1 } gann_dtype;
  *   nav_graph_prefix  directory with nav_index, nav_index.data, map.txt;
  *                     NULL or "" = enter every query at the index medoid
  *   use_gpu_mem       1: records in HBM ("-G"); 0: records in pinned host
- *                     memory, read by the GPU over the host link
+ *                     memory, read by the GPU over the host link; 2: records
+ *                     stay on storage, only the host-driven hop search
+ *                     (gann_hop_*) runs -- GustANN::init_hybrid
  *   device            CUDA device ordinal
  *   layout            0 auto, 1 PQ codes only in their own array, 2 also a
  *                     copy of every node's neighbours' codes next to its
@@ -215,6 +217,44 @@ int gann_search_noalloc(const gann_device_index* desc, const float* d_queries, i
 int gann_part_export(gann_handle* h, void* blob, int64_t blob_bytes);
 int gann_part_attach(gann_handle* h, int32_t part, const void* blob, int64_t blob_bytes);
 
+/*
+ * Host-driven search, one hop per call: the reference's SSD-hybrid mode
+ * (GustANN::init_hybrid + HybridExecutor, src/hybrid.cu; per-hop kernels
+ * src/impl/hyd_search_v2.cuh:8-472 driven by src/hyd_task_runner.cu:12-329),
+ * for indexes whose node records stay on storage. PQ codes, pivots and the
+ * pivot graph are in HBM (a handle opened as usual); the caller reads, between
+ * hops, the 4 KB page that holds each query's requested node -- page
+ * 1 + id / nodes_per_page of the disk index (gann_read_pages does this with
+ * pread) -- and hands the pages to gann_hop_step. As in the reference's hybrid
+ * mode, the pivot-graph entry and the re-rank use q'' = (q - c) + c.
+ *   gann_hop_begin     stage nq queries (host, float32 [nq x dim]); entries found
+ *   gann_hop_requests  node id each query needs next, -1 when it is done
+ *                      (host int32 [nq]); *active = number of ids >= 0
+ *   gann_hop_step      advance every active query by one hop; pages = host
+ *                      [nq x 4096] with row i = the page of node_ids[i] (rows of
+ *                      finished queries are ignored)
+ *   gann_hop_finish    results, as gann_search writes them
+ *   gann_hop_free      release the batch (the handle stays open)
+ * Needs dim * element size and the record length to be multiples of 4 bytes.
+ * The handle must outlive its batches and is not used by other calls meanwhile.
+ */
+typedef struct gann_hop_batch gann_hop_batch;
+int gann_hop_begin(gann_handle* h, const float* queries, int64_t nq, int32_t topk, int32_t ef_search,
+                   gann_hop_batch** out);
+int gann_hop_requests(gann_hop_batch* b, int32_t* node_ids, int64_t* active);
+int gann_hop_step(gann_hop_batch* b, const void* pages);
+int gann_hop_finish(gann_hop_batch* b, int32_t* nns, float* distances, int32_t* found_cnt);
+int gann_hop_free(gann_hop_batch* b);
+
+/* Storage loader for the host-driven search: reads, for each of n node ids,
+ * the 4 KB page holding its record from a disk index (page 1 + id /
+ * nodes_per_page) into pages[i * 4096], with `threads` reader threads (<= 0:
+ * hardware concurrency). Ids < 0 leave their row untouched. Host only. Takes
+ * the place of the reference's IO backends for a file on a local disk
+ * (src/io/interface.hpp:10-40, src/io/mem_io.cpp:11-51). */
+int gann_read_pages(const char* index_file, const int32_t* node_ids, int64_t n, int32_t nodes_per_page,
+                    void* pages, int32_t threads);
+
 /* Release device and host memory of the handle (GustANN::~GustANN,
  * src/ssd_search.cu:112-137). NULL is accepted. */
 int gann_close(gann_handle* h);
@@ -224,7 +264,7 @@ int gann_close(gann_handle* h);
  *     PQ pivot table resident once per SM with table entries recomputed per
  *     lookup (bit-identical sums; needs <= 4 dims per chunk and D <= 128).
  *     Auto picks 2 when it fits.
- *   GANN_OPT_PIVOT_WARPS: queries in flight per SM in mode 2 (8..20, 0 auto).
+ *   GANN_OPT_PIVOT_WARPS: queries in flight per SM in mode 2 (8..24, 0 auto).
  *   GANN_OPT_NEIGHBOUR_CODES: 1 read neighbour codes from the per-node copy
  *     when the handle has one (layout 0/2), 0 from the shared code array. */
 enum { GANN_OPT_ADC_MODE = 1, GANN_OPT_PIVOT_WARPS = 2, GANN_OPT_NEIGHBOUR_CODES = 3 };

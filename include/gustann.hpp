@@ -1,10 +1,11 @@
 // gustann.hpp -- header-only C++ facade over the C ABI (gann.h) with the
 // reference's host API, so a driver written against gustann::GustANN
 // (src/ssd_search.hpp:18-83) compiles and links against libgann.so unchanged
-// for the in-memory modes. Errors throw std::runtime_error, as the reference's
+// for the in-memory and hybrid modes. Errors throw std::runtime_error, as the reference's
 // CHECK_CUDA does (src/common_cuda.cuh:10-17).
 #pragma once
 
+#include <chrono>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -34,7 +35,9 @@ struct GustANNStats {
   long long bytes_touched = 0;
 };
 
-// src/hybrid_config.hpp:8-19; accepted for source compatibility only
+// src/hybrid_config.hpp:8-19. mini_batch (> 0: queries per hop batch) and
+// thread_cnt (page reader threads) are used; the IO backend is always a
+// threaded pread of the local index file (src/io/mem_io.cpp's role).
 struct HybridExecutorConfig {
   int mini_batch = 0;
   int thread_cnt = 0;
@@ -62,17 +65,36 @@ class GustANN {
     c.use_gpu_mem = use_gpu_mem ? 1 : 0;
     c.device = device_;
     check(gann_open(&c, &h_));
+    is_hybrid_ = false;
   }
 
-  // The SSD-tiered executor (src/hybrid.cu) is not part of this build.
-  void init_hybrid(const GustANNConfig&, const HybridExecutorConfig&) {
-    throw std::runtime_error("GANN_EUNSUPPORTED: init_hybrid is not provided by this build");
+  // src/ssd_search.cu:81-106: node records stay in the index file; search()
+  // then drives the host-driven hop search (gann_hop_*), reading the page of
+  // every query's next node between hops.
+  void init_hybrid(const GustANNConfig& config, const HybridExecutorConfig& hc) {
+    gann_close(h_);
+    h_ = nullptr;
+    index_file_ = config.index_file;
+    gann_config c{};
+    c.index_file = config.index_file.c_str();
+    c.pq_file_prefix = config.pq_file_prefix.c_str();
+    c.nav_graph_prefix = config.nav_graph_prefix.c_str();
+    c.dtype = data_type_;
+    c.use_gpu_mem = 2;
+    c.device = device_;
+    check(gann_open(&c, &h_));
+    hybrid_ = hc;
+    is_hybrid_ = true;
   }
 
   // src/ssd_search.cu:114-140
   void search(const float* qdata, const int num_queries, const int topk, const int ef_search, int* nns,
               float* distances, int* found_cnt, GustANNStats* stats = nullptr) {
     if (!h_) throw std::runtime_error("GANN_ESTATE: search before init_pure_mem");
+    if (is_hybrid_) {
+      search_hybrid(qdata, num_queries, topk, ef_search, nns, distances, found_cnt, stats);
+      return;
+    }
     gann_stats st{};
     check(gann_search(h_, qdata, num_queries, topk, ef_search, nns, distances, found_cnt, &st));
     if (stats) {
@@ -88,12 +110,55 @@ class GustANN {
   gann_handle* handle() const { return h_; }
 
  private:
+  void search_hybrid(const float* qdata, int nq, int topk, int ef, int* nns, float* distances, int* found_cnt,
+                     GustANNStats* stats) {
+    const auto t0 = std::chrono::steady_clock::now();
+    gann_info info{};
+    check(gann_index_info(h_, &info));
+    const int batch = hybrid_.mini_batch > 0 ? hybrid_.mini_batch : (nq > 0 ? nq : 1);
+    std::vector<int32_t> ids;
+    std::vector<unsigned char> pages;
+    long long hops = 0;
+    for (int lo = 0; lo < nq; lo += batch) {
+      const int n = nq - lo < batch ? nq - lo : batch;
+      gann_hop_batch* b = nullptr;
+      check(gann_hop_begin(h_, qdata + static_cast<size_t>(lo) * info.dim, n, topk, ef, &b));
+      ids.assign(n, -1);
+      pages.assign(static_cast<size_t>(n) * 4096, 0);
+      int rc = GANN_OK;
+      for (;;) {
+        int64_t active = 0;
+        if ((rc = gann_hop_requests(b, ids.data(), &active)) != GANN_OK || active == 0) break;
+        if ((rc = gann_read_pages(index_file_.c_str(), ids.data(), n, info.nodes_per_page, pages.data(),
+                                  hybrid_.thread_cnt)) != GANN_OK) break;
+        if ((rc = gann_hop_step(b, pages.data())) != GANN_OK) break;
+        ++hops;
+      }
+      if (rc == GANN_OK)
+        rc = gann_hop_finish(b, nns + static_cast<size_t>(lo) * topk, distances + static_cast<size_t>(lo) * topk,
+                             found_cnt + lo);
+      gann_hop_free(b);
+      check(rc);
+    }
+    if (stats) {
+      *stats = GustANNStats();
+      // wall time of the whole hop loop: entry search, page reads and hops
+      stats->run_time = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      stats->total_time = stats->run_time;
+      stats->hops = hops;   // hop rounds (one page read per active query each)
+    }
+  }
+
+
   static void check(int rc) {
     if (rc != GANN_OK) throw std::runtime_error(std::string("gann error ") + std::to_string(rc) + ": " + gann_last_error());
   }
   DataType data_type_;
   int device_;
   gann_handle* h_ = nullptr;
+  bool is_hybrid_ = false;
+  HybridExecutorConfig hybrid_;
+  std::string index_file_;
 };
 
 }  // namespace gustann

@@ -158,10 +158,13 @@ def test_use_before_init():
     assert e.value.code == api.GANN_ESTATE
 
 
-def test_hybrid_is_unsupported():
+def test_hybrid_open_parses_files_first(tmp_path):
+    """init_hybrid (records left on storage) validates the files like init_pure_mem."""
+    p = _copy_golden(tmp_path)
+    g = GustANN(formats.UINT8)
     with pytest.raises(GustANNError) as e:
-        GustANN().init_hybrid(None, None)
-    assert e.value.code == api.GANN_EUNSUPPORTED
+        g.init_hybrid(GustANNConfig(str(tmp_path / "nope"), p["pq_file_prefix"], p["nav_graph_prefix"]))
+    assert e.value.code == api.GANN_EIO
 
 
 def test_cli_usage_and_errors():
