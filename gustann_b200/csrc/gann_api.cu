@@ -242,6 +242,7 @@ int load_parts(gann_handle* h, const gann_config* cfg) {
   while ((static_cast<int64_t>(h->part_count) << shift) < hi.num_points) ++shift;
   ix.nparts = h->part_count;
   ix.part_shift = shift;
+  ix.local_part = h->part_index;
   ix.vec_stride = gann::round_up(hi.dim, 32) * hi.elem;
   ix.adj_stride = static_cast<int32_t>(gann::round_up(hi.max_m0, 4));
   // neighbour codes per range, on the same rule as the single layout,

@@ -78,6 +78,7 @@ struct DeviceIndex {
   // reached through peer pointers); vecs/adj/ncodes above are then unused
   int32_t nparts = 0;
   int32_t part_shift = 0;
+  int32_t local_part = -1;  // the range in this GPU's memory (-1: every range)
   const uint8_t* part_vecs[kMaxParts] = {};
   const uint32_t* part_adj[kMaxParts] = {};
   const uint8_t* part_ncodes[kMaxParts] = {};

@@ -358,7 +358,9 @@ __device__ __forceinline__ const uint8_t* ncode_row(const DeviceIndex& ix, uint3
 // (dims l, l+32, ...) of one record. With the neighbour-code layout the node's
 // block of neighbour code rows, whose address depends only on the node, is
 // prefetched into L2 (no registers held while the merge runs; the hop that
-// expands the node loads the rows it needs from L2).
+// expands the node loads the rows it needs from L2) -- when the block is in
+// this GPU's memory: an L2 prefetch of a peer GPU's address made split-record
+// searches ~50x slower on B200, so remote blocks are simply loaded.
 template <typename T, int NPL, int VP>
 __device__ __forceinline__ void load_node(const DeviceIndex& ix, uint32_t u, int lane, uint32_t (&nb)[NPL],
                                           float (&xv)[VP]) {
@@ -368,7 +370,8 @@ __device__ __forceinline__ void load_node(const DeviceIndex& ix, uint32_t u, int
     const int e = lane + kWarp * k;
     nb[k] = e < ix.degree ? __ldg(arow + e) : kPadId;
   }
-  if (ix.ncodes != nullptr) {
+  const bool local = ix.nparts <= 1 || ix.local_part < 0 || static_cast<int>(u >> ix.part_shift) == ix.local_part;
+  if (ix.ncodes != nullptr && local) {
     const uint8_t* crow = ncode_row(ix, u);
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
