@@ -259,7 +259,7 @@ __device__ __forceinline__ float adc16_piv(float s, const uint4 c, const PivTab&
   for (int b = 0; b < 16; ++b) {
     if (b < n) {
       const float4 q = qcp[b];
-      const int r = row0 + b * kPivots + static_cast<int>((w[b >> 2] >> (8 * (b & 3))) & 0xffu);
+      const int r = row0 + b * kPivots + static_cast<int>(__byte_perm(w[b >> 2], 0u, 0x4440u | (b & 3)));
       float4 p;
       if (CW == 3) {
         const float2 xy = t.xy[r];
@@ -267,11 +267,15 @@ __device__ __forceinline__ float adc16_piv(float s, const uint4 c, const PivTab&
       } else {
         p = t.xyzw[r];
       }
-      float d = __fsub_rn(q.x, p.x);
-      float e = __fmul_rn(d, d);
-      d = __fsub_rn(q.y, p.y);
-      e = __fmaf_rn(d, d, e);
-      d = __fsub_rn(q.z, p.z);
+      // the x and y differences in one packed instruction (two independent
+      // round-to-nearest subtractions, as __fsub_rn would give)
+      float dx, dy;
+      asm("{.reg .b64 a, b, c;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+          "sub.rn.f32x2 c, a, b;\n\tmov.b64 {%0, %1}, c;}"
+          : "=f"(dx), "=f"(dy) : "f"(q.x), "f"(q.y), "f"(p.x), "f"(p.y));
+      float e = __fmul_rn(dx, dx);
+      e = __fmaf_rn(dy, dy, e);
+      float d = __fsub_rn(q.z, p.z);
       e = __fmaf_rn(d, d, e);
       if (CW > 3) {
         d = __fsub_rn(q.w, p.w);
