@@ -551,7 +551,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       rk[k] = 0;
       if (ok[k] && (key[k] >> 1) >= last) ok[k] = false;
     }
-    if (psize > 0) {
+    if (psize > 0 && cnt > kWarp) {
       for (int step = 1 << (31 - __clz(psize)); step > 0; step >>= 1) {
 #pragma unroll
         for (int k = 0; k < NPL; ++k) {
@@ -559,16 +559,25 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
           if (ok[k] && t <= psize && (s.pool[t - 1] >> 1) < (key[k] >> 1)) rk[k] = t;
         }
       }
+    } else if (psize > 0) {
+      // at most 32 neighbours were evaluated: only the first pass holds any
+      for (int step = 1 << (31 - __clz(psize)); step > 0; step >>= 1) {
+        const int t = rk[0] + step;
+        if (ok[0] && t <= psize && (s.pool[t - 1] >> 1) < (key[0] >> 1)) rk[0] = t;
+      }
     }
 #pragma unroll
     for (int k = 0; k < NPL; ++k) {
       if (ok[k] && rk[k] < psize && (s.pool[rk[k]] >> 1) == (key[k] >> 1)) ok[k] = false;
       if (ok[k] && key[k] < mk) mk = key[k];
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const uint64_t o = __shfl_xor_sync(kFull, mk, off);
-      mk = o < mk ? o : mk;
+    {
+      // warp minimum of the 64-bit keys: the high words, then the low words of
+      // the lanes holding that high word (two redux.sync instead of 5 shuffle rounds)
+      const uint32_t mhi = __reduce_min_sync(kFull, static_cast<uint32_t>(mk >> 32));
+      const uint32_t mlo = __reduce_min_sync(kFull, static_cast<uint32_t>(mk >> 32) == mhi
+                                                        ? static_cast<uint32_t>(mk) : 0xffffffffu);
+      mk = (static_cast<uint64_t>(mhi) << 32) | mlo;
     }
     const uint64_t nxt = mk < pstar ? mk : pstar;
     const bool more = nxt != ~0ull;
@@ -665,7 +674,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
         }
       }
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) rmin = min(rmin, __shfl_xor_sync(kFull, rmin, off));
+      rmin = __reduce_min_sync(kFull, rmin);
       // survivor ranks in key order are non-decreasing: hist[t] = rank of the
       // t-th smallest survivor; entry i >= rmin moves right by #{t : hist[t] <= i}
 #pragma unroll
