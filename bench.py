@@ -51,7 +51,10 @@ def parse():
                     help="override the number of base points (use --points under torchrun: its parser takes --n)")
     ap.add_argument("--nq", type=int, default=10000)
     ap.add_argument("--target", type=float, default=0.9)
-    ap.add_argument("--efs", default="32,48,64,80,96,112,128,144,160,176,192,224,256,320,384,448,512,640,768,1024")
+    # the sweep stops at the first ef reaching the recall target; steps of 8
+    # around the C1 operating point keep that ef close to the smallest that does
+    ap.add_argument("--efs", default="32,48,64,80,96,112,128,136,144,152,160,168,176,184,192,200,208,224,240,256,"
+                                     "288,320,384,448,512,640,768,1024")
     ap.add_argument("--cache", default=os.environ.get("GANN_BENCH_CACHE", "/tmp/gann_bench"))
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
