@@ -185,24 +185,30 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def traffic_per_launch(cfg_key: str, n: int, ef: int):
+def traffic_per_launch(cfg_key: str, n: int, ef: int, hops: int):
     """DRAM bytes (read + write) per launch of the search kernel, from a
-    committed ncu summary under profiles/ that names this workload:
-    a line `traffic_bytes_per_launch <config> n=<points> ef=<ef>: <bytes>`.
-    None when no capture of this exact workload was committed."""
+    committed ncu summary under profiles/ that names this workload: a line
+    `traffic_bytes_per_launch <config> n=<points> ef=<ef> hops=<hops>: <bytes>`.
+    The capture at the nearest ef is scaled by expanded nodes (the traffic is
+    per hop: one record and one neighbour-code block); the index is rebuilt on
+    every machine, so even a capture at the same ef is scaled by this run's
+    expanded nodes. Returns (bytes, source) or (None, reason)."""
     d = os.path.join(ROOT, "profiles")
-    pat = re.compile(r"^traffic_bytes_per_launch (\S+) n=(\d+) ef=(\d+): (\d+)\s*$")
-    if not os.path.isdir(d):
-        return None
-    for name in sorted(os.listdir(d)):
-        if not name.endswith(".md"):
-            continue
-        with open(os.path.join(d, name)) as f:
-            for line in f:
-                m = pat.match(line.strip())
-                if m and m.group(1) == cfg_key and int(m.group(2)) == n and int(m.group(3)) == ef:
-                    return int(m.group(4))
-    return None
+    pat = re.compile(r"^traffic_bytes_per_launch (\S+) n=(\d+) ef=(\d+) hops=(\d+): (\d+)\s*$")
+    found = []
+    if os.path.isdir(d):
+        for name in sorted(os.listdir(d)):
+            if not name.endswith(".md"):
+                continue
+            with open(os.path.join(d, name)) as f:
+                for line in f:
+                    m = pat.match(line.strip())
+                    if m and m.group(1) == cfg_key and int(m.group(2)) == n:
+                        found.append((int(m.group(3)), int(m.group(4)), int(m.group(5)), name))
+    if found and hops > 0:
+        e, h, b, name = min(found, key=lambda t: abs(t[0] - ef))
+        return int(b * hops / h), f"ncu capture at ef={e} (profiles/{name}) scaled by expanded nodes {hops}/{h}"
+    return None, "no ncu capture of this index committed"
 
 
 # ------------------------------------------------------------------ data
@@ -432,9 +438,10 @@ def run_ours(args, d: Dist):
 
     peak, peak_kind = measured_peak()
     achieved = st.bytes_touched / (np.mean(step_ms) * 1e-3) / 1e9
-    traffic = traffic_per_launch(args.config, spec.n, ef)
+    traffic, traffic_src = traffic_per_launch(args.config, spec.n, ef, int(st.hops))
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+            "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
+            "peak_kind": peak_kind,
             "algorithmic_bytes_per_launch": int(st.bytes_touched),
             "hops_per_query": st.hops / nq, "adc_per_query": st.adc_evals / nq}
 
