@@ -292,12 +292,12 @@ struct WarpSmem {
   float4* qcp;    // per-chunk query residuals, 4 dims padded (pivot mode)
   float* qs;      // q, then q'' = (q - c) + c once the entry is known
   float* qc;      // q - c
-  uint64_t* pool;
-  uint64_t* cand;
-  int* candr;
-  int* hist;       // survivor ranks in key order (merge)
-  float* topd;
-  int* topi;
+  uint64_t* pool;  // up to ef keys, sorted
+  uint64_t* cand;  // survivors' keys (merge)
+  int* candr;      // survivors' pool ranks (merge); compacted neighbour ids at hop start
+  int* hist;       // survivor ranks in key order (merge); compacted neighbour slots at hop start
+  float* topd;     // top-k exact distances
+  int* topi;       // top-k ids
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
