@@ -1,0 +1,61 @@
+"""Host-side pieces of bench.py that shape its JSON line: recall@k, the traffic
+figure read from the committed ncu summary, and the clock-sample filter."""
+import os
+import sys
+
+import numpy as np
+
+from conftest import ROOT
+
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+
+def test_recall_at_counts_set_intersection():
+    nns = np.array([[1, 2, 3], [4, 5, 6]])
+    gt = np.array([[3, 2, 9], [7, 8, 9]])
+    assert bench.recall_at(nns, gt, k=3) == 2 / 6
+    assert bench.recall_at(nns, nns, k=3) == 1.0
+
+
+def test_traffic_scales_the_committed_capture_by_hops():
+    b, src = bench.traffic_per_launch("c1", 10_000_000, 176, 0)
+    assert b is None
+    lines = [ln for ln in open(os.path.join(ROOT, "profiles", "search_kernel_piv_c1_10m_launch_list.md"))
+             if ln.startswith("traffic_bytes_per_launch c1 n=10000000")]
+    assert len(lines) == 1
+    head, val = lines[0].rsplit(":", 1)
+    hops = int(head.split("hops=")[1])
+    base = int(val)
+    b, src = bench.traffic_per_launch("c1", 10_000_000, 176, hops)
+    assert b == base and "ef=176" in src
+    b2, _ = bench.traffic_per_launch("c1", 10_000_000, 192, 2 * hops)
+    assert b2 == 2 * base
+    assert bench.traffic_per_launch("c1", 123, 176, hops)[0] is None
+
+
+def test_clock_samples_inside_the_window():
+    c = bench.Clocks.__new__(bench.Clocks)
+    c.p = None
+    c.lines = []
+    assert c.stop(0.0, 1.0)["samples"] == 0                     # no sampler
+
+    class Done:
+        def terminate(self):
+            pass
+
+        def wait(self, timeout=None):
+            return 0
+
+    row = "0, {mhz}, 1965, 700.0, 0x0, Not Active, Not Active, Not Active, {cap}"
+    c.p = Done()
+    c.lines = [(0.5, row.format(mhz=1000, cap="Not Active")),
+               (1.01, row.format(mhz=1965, cap="Active")),
+               (1.02, row.format(mhz=1965, cap="Not Active")),
+               (3.0, row.format(mhz=900, cap="Not Active"))]
+    r = c.stop(1.0, 1.03)
+    assert r["samples"] == 2 and r["sm_mhz"] == 1965 and r["reasons"] == ["sw_power_cap"]
+    assert r["window"] == "inside the timed region"
+    c.lines = [(0.5, row.format(mhz=1500, cap="Not Active")), (3.0, row.format(mhz=1600, cap="Not Active"))]
+    r = c.stop(1.0, 1.001)
+    assert r["samples"] == 2 and r["window"].startswith("nearest")
