@@ -11,8 +11,9 @@ smallest survivor rank's chunk, and the first-unvisited lower bound -- so that
 changes to those
 mechanics can be checked on the CPU against `reference_expansions`, a literal
 model of the reference's merge-path / 2L-cut / dedup / first-unvisited step
-(src/impl/pure_mem.cuh:314-419). Both return the sequence of expanded node ids;
-the top-k re-rank does not influence it.
+(src/impl/pure_mem.cuh:314-419). `hop_expansions` models the count-based merge
+of hop_step_kernel (the host-driven hop search). All return the sequence of
+expanded node ids; the top-k re-rank does not influence it.
 
 ADC values come from the oracle's bit-exact tables, summed in float32 in chunk
 order, exactly as both implementations do.
@@ -209,4 +210,45 @@ def kernel_expansions(entry, neighbours, adc, L, max_hops=1 << 14, vis_bits=11, 
         if not more:
             return out
         u = (nxt & 0xFFFFFFFF) >> 1
+    return out
+
+
+def hop_expansions(entry, neighbours, adc, L, max_hops=1 << 14):
+    """Model of hop_step_kernel (the host-driven hop search, one launch per
+    hop): neighbours equal to a pool entry are dropped; the merged pool puts
+    pool entry i at i + #(survivors below it) and survivor e at #(survivors
+    below it, ties by slot) + #(pool entries below it), keeps the first L, and
+    requests its first unvisited entry (none: done). Returns the expanded ids."""
+    pool: list[int] = []
+    u = entry
+    out = []
+    for _ in range(max_hops):
+        out.append(u)
+        nb = list(neighbours(u))
+        dn = adc(nb).tolist() if nb else []
+        nk = [key_of(np.float32(d), v) for d, v in zip(dn, nb)]
+        ps = len(pool)
+        pk = [p >> 1 for p in pool]
+        for e, k in enumerate(nk):
+            kk = k >> 1
+            lo = sum(1 for p in pk if p < kk)     # lower bound in the sorted pool
+            if lo < ps and pk[lo] == kk:
+                nk[e] = None
+        surv = [(e, k) for e, k in enumerate(nk) if k is not None]
+        nsz = min(ps + len(surv), L)
+        mg = [None] * (ps + len(surv))
+        for i, p in enumerate(pool):
+            below = sum(1 for _, k in surv if (k >> 1) < (p >> 1))
+            mg[i + below] = p
+        for e, k in surv:
+            below = sum(1 for f, o in surv if (o >> 1) < (k >> 1) or ((o >> 1) == (k >> 1) and f < e))
+            lo = sum(1 for p in pk if p < (k >> 1))
+            mg[below + lo] = k
+        mg = mg[:nsz]
+        first = next((j for j, k in enumerate(mg) if k & 1), None)
+        if first is None:
+            return out
+        mg[first] &= ~1
+        pool = mg
+        u = (mg[first] & 0xFFFFFFFF) >> 1
     return out

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 from gustann_b200 import formats
-from kernel_model import adc_sums, kernel_expansions, reference_expansions
+from kernel_model import adc_sums, hop_expansions, kernel_expansions, reference_expansions
 from oracle import Oracle
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -46,3 +46,23 @@ def test_kernel_mechanics_equal_reference_merge(name, ef, vis_bits, pool_filter)
         assert ker == ref, f"query {t}: expansions differ"
         assert len(ref) == hops[t]
         assert stale == bool(flags[t] & 2)
+
+
+@pytest.mark.parametrize("name", list(GOLD))
+@pytest.mark.parametrize("ef", [10, 33, 64])
+def test_hop_kernel_merge_equals_reference_merge(name, ef):
+    """hop_step_kernel's count-based merge expands the reference's sequence."""
+    o, deg, nbrs, codes, q = _load(name)
+    luts = o.lut(q[:16])
+    _, entries, _ = o.nav(q[:16])
+    for t in range(16):
+        lut = luts[t]
+
+        def neighbours(u):
+            return nbrs[u, : deg[u]].tolist()
+
+        def adc(ids):
+            return adc_sums(lut, codes, ids)
+
+        ref, stale = reference_expansions(int(entries[t]), neighbours, adc, ef)
+        assert hop_expansions(int(entries[t]), neighbours, adc, ef) == ref, f"query {t}"
