@@ -528,6 +528,13 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
 #pragma unroll
         for (int k = 0; k < NPL; ++k)
           if (ok[k]) dsum[k] = adc16(dsum[k], cur[k], lw, n);
+      } else if (n == 16) {
+        // a full word: the chunk bound folds away (the common case, M % 16 == 0)
+        const float4* qw = s.qcp + 16 * w;
+#pragma unroll
+        for (int k = 0; k < NPL; ++k)
+          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, 16)
+                                        : adc16_piv<4>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, 16);
       } else {
         const float4* qw = s.qcp + 16 * w;
 #pragma unroll
