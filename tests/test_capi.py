@@ -46,6 +46,26 @@ def test_header_compiles_as_c_and_cpp(tmp_path):
                     "-o", str(tmp_path / "t2.o")], check=True)
 
 
+def test_facade_program_links_against_the_library(tmp_path):
+    """A driver written against gustann::GustANN (in-HBM and hybrid modes)
+    compiles and links against libgann.so (not run: no GPU here)."""
+    src = tmp_path / "drv.cpp"
+    src.write_text(
+        '#include "gustann.hpp"\n'
+        "int main(int argc, char** argv) {\n"
+        "  gustann::GustANN a(gustann::FLOAT);\n"
+        "  gustann::GustANNConfig c; c.index_file = argv[0]; c.pq_file_prefix = argv[0];\n"
+        "  gustann::HybridExecutorConfig h; h.mini_batch = 64; h.thread_cnt = 4;\n"
+        "  try { if (argc > 5) a.init_hybrid(c, h); else a.init_pure_mem(c, true); }\n"
+        "  catch (const std::exception&) { return 0; }\n"
+        "  float q[4] = {0}; int n[1]; float d[1]; int f[1]; gustann::GustANNStats st;\n"
+        "  a.search(q, 1, 1, 1, n, d, f, &st);\n"
+        "  return 0;\n}\n")
+    lib_dir = os.path.dirname(api.LIB_PATH)
+    subprocess.run(["g++", "-std=c++17", "-Wall", "-Werror", "-I", os.path.dirname(HEADER), str(src), "-o",
+                    str(tmp_path / "drv"), "-L", lib_dir, "-lgann", f"-Wl,-rpath,{lib_dir}"], check=True)
+
+
 def test_pivot_sample_matches_std_shuffle_semantics():
     a = api.pivot_sample(1000, 100)
     b = api.pivot_sample(1000, 100)
