@@ -1,19 +1,25 @@
 #!/usr/bin/env python
 """Benchmark: QPS at recall@10 = 0.9 of the in-HBM search path.
 
-One step = one search of the rank's query batch (10k queries, top-10) at the
-smallest swept ef_search whose recall@10 against exact ground truth reaches
-the target. Workload: configuration 1 (10M x 96-d float32, DEEP-like mixture,
-Vamana-style R=64 graph, PQ M=32, pivot graph) on one B200 per rank; ranks
-shard the queries (weak scaling, no collective on the data path).
+Workload (default): configuration 2 -- 100M x 128-d uint8 SIFT-like mixture
+(10k centers, sigma 20), Vamana graph R = 64, alpha 1.2, PQ M = 32, pivot graph
+over a 1M sample; 100k queries from the same mixture (separate seed) sharded
+across the ranks, top-10, L2. One step = one search of the rank's query shard
+at the smallest swept ef_search whose recall@10 (exact ground truth) reaches
+the target. Ranks shard the queries; the index is replicated; no collective
+runs on the data path.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config c2]
 
-Prints one JSON line (rank 0). `value` is device-resident throughput (inputs
-in HBM, CUDA events on the launching stream, max over ranks); `e2e` is the
-same metric through the C ABI with host buffers (host<->device copies inside
-the timed region). The index (6.7 GB) exceeds the 126 MB L2, so no flush is
-needed between steps.
+Prints one JSON line (rank 0). `value` is device-resident throughput (inputs in
+HBM, CUDA events on the launching stream, max over ranks); `e2e` is the same
+metric through the C ABI with host buffers (host<->device copies inside the
+timed region). The index (41 GB of records) exceeds the 126 MB L2, so no flush
+is needed between steps.
+
+The index, queries and ground truth are made once per machine by
+``python -m gustann_b200.index.make`` in a child process and cached; both arms
+read the same files.
 """
 from __future__ import annotations
 
@@ -33,40 +39,66 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from gustann_b200 import formats  # noqa: E402
-from gustann_b200.index import datagen, pipeline  # noqa: E402
-from gustann_b200.index.graph import knn_exact  # noqa: E402
+from gustann_b200.index import datagen  # noqa: E402
 
 METRIC = "QPS at recall@10=0.9 (in-HBM beam search, 1 query batch per step)"
 TOPK = 10
 
+# per-configuration defaults: total queries (sharded over the ranks) and the
+# ef_search sweep (ascending; the operating point is the first ef reaching the
+# target, so the steps are fine where the target is usually met)
+DEFAULTS = {
+    "c0": dict(nq=10_000, efs="20,24,28,32,40,48,56,64,80,96,112,128,160,192,256"),
+    "c1": dict(nq=10_000, efs="32,48,64,80,96,112,128,136,144,152,160,168,176,184,192,200,208,224,240,256,288,320,"
+                              "384,448,512,640,768,1024"),
+    "c2": dict(nq=100_000, efs="16,20,24,28,32,36,40,44,48,56,64,72,80,88,96,104,112,128,144,160,192,224,256,320,"
+                               "384,512"),
+}
+RECALL_QUERIES = 10_000   # queries whose recall chooses the operating point (the first of the set)
 
-def parse():
+
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c1", choices=list(datagen.CONFIGS))
+    ap.add_argument("--config", default="c2", choices=list(DEFAULTS))
     ap.add_argument("--points", "--n", dest="n", type=int, default=0,
                     help="override the number of base points (use --points under torchrun: its parser takes --n)")
-    ap.add_argument("--nq", type=int, default=10000)
+    ap.add_argument("--nq", type=int, default=0, help="total queries over all ranks (0: the configuration's)")
     ap.add_argument("--target", type=float, default=0.9)
-    # the sweep stops at the first ef reaching the recall target; steps of 8
-    # around the C1 operating point keep that ef close to the smallest that does
-    ap.add_argument("--efs", default="32,48,64,80,96,112,128,136,144,152,160,168,176,184,192,200,208,224,240,256,"
-                                     "288,320,384,448,512,640,768,1024")
+    ap.add_argument("--efs", default="")
+    ap.add_argument("--passes", type=int, default=0, help="Vamana passes of the index build (0: 1 above 20M points)")
     ap.add_argument("--cache", default=os.environ.get("GANN_BENCH_CACHE", "/tmp/gann_bench"))
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--parity-queries", type=int, default=2000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true")
     ap.add_argument("--split-records", action="store_true",
                     help="N>1: each rank holds 1/N of the node records and reads the others over NVLink")
-    return ap.parse_args()
+    a = ap.parse_args(argv)
+    d = DEFAULTS[a.config]
+    a.nq = a.nq or d["nq"]
+    a.efs = a.efs or d["efs"]
+    return a
 
 
 def spec_for(args) -> datagen.MixtureSpec:
     import dataclasses
     s = datagen.CONFIGS[args.config]
     return dataclasses.replace(s, n=args.n or s.n)
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 # ------------------------------------------------------------------ plumbing
@@ -79,7 +111,7 @@ class Dist:
         if self.world > 1:
             import datetime
             torch.cuda.set_device(self.local)
-            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(minutes=10),
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(minutes=30),
                                                  device_id=torch.device("cuda", self.local))
             self.pg = True
         elif torch.cuda.is_available():
@@ -89,19 +121,18 @@ class Dist:
         if self.pg:
             torch.distributed.barrier()
 
-    def max(self, x: float) -> float:
+    def reduce(self, x: float, op) -> float:
         if not self.pg:
             return x
         t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(t, op=op)
         return float(t.item())
 
+    def max(self, x: float) -> float:
+        return self.reduce(x, torch.distributed.ReduceOp.MAX if self.pg else None)
+
     def sum(self, x: float) -> float:
-        if not self.pg:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        torch.distributed.all_reduce(t)
-        return float(t.item())
+        return self.reduce(x, torch.distributed.ReduceOp.SUM if self.pg else None)
 
     def close(self):
         if self.pg:
@@ -187,12 +218,13 @@ def measured_peak():
 
 def traffic_per_launch(cfg_key: str, n: int, ef: int, hops: int):
     """DRAM bytes (read + write) per launch of the search kernel, from a
-    committed ncu summary under profiles/ that names this workload: a line
+    committed ncu summary under profiles/ that names this configuration: a line
     `traffic_bytes_per_launch <config> n=<points> ef=<ef> hops=<hops>: <bytes>`.
-    The capture at the nearest ef is scaled by expanded nodes (the traffic is
-    per hop: one record and one neighbour-code block); the index is rebuilt on
-    every machine, so even a capture at the same ef is scaled by this run's
-    expanded nodes. Returns (bytes, source) or (None, reason)."""
+    The capture of the same configuration at the nearest point count, then the
+    nearest ef, is scaled by expanded nodes (the traffic is per hop: one record
+    and the neighbours' code rows); the index is rebuilt on every machine, so
+    even a capture of the same size and ef is scaled by this run's expanded
+    nodes. Returns (bytes, source) or (None, reason)."""
     d = os.path.join(ROOT, "profiles")
     pat = re.compile(r"^traffic_bytes_per_launch (\S+) n=(\d+) ef=(\d+) hops=(\d+): (\d+)\s*$")
     found = []
@@ -203,66 +235,98 @@ def traffic_per_launch(cfg_key: str, n: int, ef: int, hops: int):
             with open(os.path.join(d, name)) as f:
                 for line in f:
                     m = pat.match(line.strip())
-                    if m and m.group(1) == cfg_key and int(m.group(2)) == n:
-                        found.append((int(m.group(3)), int(m.group(4)), int(m.group(5)), name))
+                    if m and m.group(1) == cfg_key:
+                        found.append((int(m.group(2)), int(m.group(3)), int(m.group(4)), int(m.group(5)), name))
     if found and hops > 0:
-        e, h, b, name = min(found, key=lambda t: abs(t[0] - ef))
-        return int(b * hops / h), f"ncu capture at ef={e} (profiles/{name}) scaled by expanded nodes {hops}/{h}"
-    return None, "no ncu capture of this index committed"
+        pn, e, h, b, name = min(found, key=lambda t: (abs(t[0] - n), abs(t[1] - ef)))
+        size = "" if pn == n else f" of a {pn}-point index"
+        return int(b * hops / h), (f"ncu capture{size} at ef={e} (profiles/{name}) scaled by expanded nodes "
+                                   f"{hops}/{h}")
+    return None, "no ncu capture of this configuration committed"
 
 
 # ------------------------------------------------------------------ data
-def ensure_index(spec, args, d: Dist) -> dict:
-    key = f"{args.config}_n{spec.n}_R64_M32_v3"
-    root = os.path.join(args.cache, key)
+def index_root(args, spec) -> str:
+    return os.path.join(args.cache, f"{args.config}_n{spec.n}_q{args.nq}_v4")
+
+
+def passes_for(args, spec) -> int:
+    return args.passes or (1 if spec.n > 20_000_000 else 2)
+
+
+def ensure_index(args, spec, d: Dist) -> str:
+    """Directory of the cached index, queries and ground truth. Rank 0 builds
+    it in a child process (``gustann_b200.index.make``) when it is missing."""
+    root = index_root(args, spec)
     done = os.path.join(root, "DONE")
-    paths = formats.index_paths(root)
     if d.rank == 0 and not os.path.exists(done):
-        t0 = time.time()
-        X = datagen.base_vectors(spec, device="cuda")
-        pipeline.build_index(root, X, spec.dtype, R=64, alpha=1.2, M=32, nav_samples=1_000_000)
-        del X
-        torch.cuda.empty_cache()
-        with open(done, "w") as f:
-            f.write(f"{time.time() - t0:.1f}\n")
+        cmd = [sys.executable, "-m", "gustann_b200.index.make", "--config", args.config, "--root", root,
+               "--points", str(spec.n), "--nq", str(args.nq), "--passes", str(passes_for(args, spec)),
+               "--device", str(d.local)]
+        r = subprocess.run(cmd, cwd=ROOT, stdout=sys.stderr, stderr=sys.stderr)
+        if r.returncode != 0 or not os.path.exists(done):
+            raise RuntimeError(f"index build failed (rc={r.returncode}): {' '.join(cmd)}")
     t0 = time.time()
     while not os.path.exists(done):
-        if time.time() - t0 > 3600:
+        if time.time() - t0 > 7200:
             raise TimeoutError("index build by rank 0 did not finish")
         time.sleep(2)
-    return paths
+    return root
+
+
+def load_workload(root: str, spec):
+    """(paths, queries float32 [nq, D], ground truth int32 [nq, k], meta)."""
+    from gustann_b200.index.make import read_queries
+    paths = formats.index_paths(root)
+    Q = read_queries(root, spec.dtype)
+    gt = formats.read_vecs(os.path.join(root, "gt.ivecs"), np.int32)
+    with open(os.path.join(root, "meta.json")) as f:
+        meta = json.load(f)
+    return paths, Q, gt, meta
+
+
+def shard(n: int, rank: int, world: int) -> tuple[int, int]:
+    return n * rank // world, n * (rank + 1) // world
+
+
+def recall_hits(nns: np.ndarray, gt: np.ndarray, k: int = TOPK) -> int:
+    """Set-intersection hits (bin/utils.hpp:104-116: duplicate result ids each count)."""
+    hit = 0
+    for a, b in zip(nns[:, :k], gt[:, :k]):
+        s = set(b.tolist())
+        hit += sum(1 for x in a.tolist() if x in s)
+    return hit
 
 
 def recall_at(nns: np.ndarray, gt: np.ndarray, k: int = TOPK) -> float:
-    """Set-intersection recall@k (bin/utils.hpp:104-116)."""
-    hit = 0
-    for a, b in zip(nns[:, :k], gt[:, :k]):
-        hit += len(set(a.tolist()) & set(b.tolist()))
-    return hit / (len(nns) * k)
+    return recall_hits(nns, gt, k) / (len(nns) * k)
 
 
-def ground_truth(spec, Q: np.ndarray) -> np.ndarray:
-    X = datagen.base_vectors(spec, device="cuda")
-    qt = torch.from_numpy(Q).cuda()
-    ids, _ = knn_exact(X, qt, TOPK)
-    del X
-    torch.cuda.empty_cache()
-    return ids.cpu().numpy()
+def config_json(args, spec, ef, rec, passes):
+    return {"workload": f"{args.config}: {spec.n} x {spec.dim}-d {'uint8' if spec.dtype == 0 else 'float32'} "
+                        f"{spec.kind}-like mixture ({spec.centers} centers, sigma {spec.sigma:g}), Vamana R=64 "
+                        f"alpha=1.2 ({passes} pass{'es' if passes > 1 else ''}), PQ M=32, pivot graph (1M samples), "
+                        f"{args.nq} queries sharded over the ranks, top-{TOPK}, L2",
+            "ef_search": ef, "recall_at_10": rec, "recall_target": args.target, "queries_total": args.nq,
+            "l2_flush": "not needed: index larger than L2",
+            "parallelism": f"query shards x{args.gpus}, index replicated" + (
+                f", records split x{args.gpus}" if getattr(args, "split_records", False) and args.gpus > 1 else "")}
 
 
 # ------------------------------------------------------------------ arms
-def cpu_baseline(paths, dtype, Q, ef, seconds):
-    """The oracle (C restatement of the reference path) on the host cores,
-    on a bounded sample of the workload's queries."""
+def oracle_module():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as orc
     orc.build(ref=False)
-    o = orc.Oracle(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], dtype)
+    return orc
+
+
+def cpu_baseline(o, Q, ef, seconds):
+    """The oracle (C restatement of the reference path) on the host cores,
+    on a bounded sample of the workload's queries."""
     cores = os.cpu_count() or 1
     done, t_total, i = 0, 0.0, 0
     batch = max(256, 8 * cores)
-    # cycle through the workload's queries until `seconds` of CPU work (at most
-    # three passes), so a fast host still gives a stable figure
     while t_total < seconds and done < 3 * len(Q):
         qb = Q[i % len(Q): i % len(Q) + batch]
         t0 = time.perf_counter()
@@ -270,9 +334,8 @@ def cpu_baseline(paths, dtype, Q, ef, seconds):
         t_total += time.perf_counter() - t0
         done += len(qb)
         i += len(qb)
-    o.close()
-    return {"value": done / t_total, "unit": "queries/s", "cores": cores, "kind": "port",
-            "sample": f"{done} query searches over the workload's {len(Q)} queries at ef_search={ef}, "
+    return {"value": done / t_total, "unit": "queries/s", "cores": cores, "cpu_model": cpu_model(), "kind": "port",
+            "sample": f"{done} query searches over the workload's first {len(Q)} queries at ef_search={ef}, "
                       f"{t_total:.1f} s of CPU work"}
 
 
@@ -280,28 +343,36 @@ def run_reference(args, d: Dist):
     """--impl reference: the reference path's CPU restatement (the reference
     has no CPU search of its own) timed on the host cores; rank 0 only.
 
-    Also reported, as context: the reference's own CUDA kernels (compiled from
-    its sources into oracle/_ref) on this GPU, same index, queries and ef --
-    given only the queries the oracle shows inside its defined behaviour."""
+    Also, outside the timed region: the reference's own CUDA kernels (compiled
+    from its sources into oracle/_ref) on this GPU, same index and queries,
+    swept over the same ef values -- given only the queries the oracle shows
+    to be inside the reference's defined behaviour at that ef. Their results
+    and the oracle's sweep are left in the cache directory for the other arm's
+    parity report."""
     if d.rank != 0:
         return
     spec = spec_for(args)
-    paths = ensure_index(spec, args, d)
-    Q = datagen.as_float_queries(datagen.query_vectors(spec, args.nq, device="cuda", offset=0))
-    gt = ground_truth(spec, Q)
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as orc
-    orc.build(ref=False)
+    root = ensure_index(args, spec, d)
+    paths, Q, gt, meta = load_workload(root, spec)
+    passes = meta.get("passes", 2)
+    rq = min(len(Q), RECALL_QUERIES)
+    orc = oracle_module()
+    t0 = time.time()
     o = orc.Oracle(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], spec.dtype)
+    t_open = time.time() - t0
     cores = os.cpu_count() or 1
     efs = [int(x) for x in args.efs.split(",")]
-    ef, rec, flags = efs[-1], 0.0, None
+    ef, rec = efs[-1], 0.0
+    sweep, flags_at = [], {}
     for e in efs:
-        nns, _, _, _, fl = o.search(Q, TOPK, e, threads=cores)
-        rec, flags = recall_at(nns, gt), fl
-        if rec >= args.target:
-            ef = e
+        nns, _, _, _, fl = o.search(Q[:rq], TOPK, e, threads=cores)
+        r = recall_at(nns, gt[:rq])
+        sweep.append((e, round(r, 5)))
+        flags_at[e] = fl
+        if r >= args.target:
+            ef, rec = e, r
             break
+        rec = r
     per_step = min(len(Q), 2000)
     for _ in range(args.warmup):
         o.search(Q[:min(per_step, 256)], TOPK, ef, threads=cores)
@@ -316,47 +387,75 @@ def run_reference(args, d: Dist):
     tot_q = sum(n for _, n in times)
     v = tot_q / tot_t
     ref_gpu = None
-    if orc.RefGPU.available():
-        clean = Q[flags == 0]
+    if orc.RefGPU.available() and not args.no_reference_gpu:
+        t0 = time.time()
         r = orc.RefGPU(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], spec.dtype, spec.dim)
-        r.search(clean, TOPK, ef)
-        rts = [r.search(clean, TOPK, ef)[3] for _ in range(args.steps)]
+        t_ref_open = time.time() - t0
+        rsweep, keep = [], {}
+        for e, _ in sweep:
+            clean = np.nonzero(flags_at[e] == 0)[0]
+            rn, rd, rf, _ = r.search(Q[clean], TOPK, e)
+            rsweep.append((e, round(recall_at(rn, gt[clean]), 5), int(len(clean))))
+            keep[e] = (clean, rn, rd, rf)
+        clean, rn, rd, rf = keep[ef]
+        r.search(Q[clean], TOPK, ef)
+        rts = [r.search(Q[clean], TOPK, ef)[3] for _ in range(args.steps)]
         r.close()
+        np.savez(os.path.join(root, f"refgpu_ef{ef}.npz"), idx=clean, nns=rn, dist=rd, found=rf)
         ref_gpu = {"value": len(clean) / float(np.mean(rts)), "unit": "queries/s", "ef_search": ef,
-                   "queries": int(len(clean)),
+                   "queries": int(len(clean)), "load_s": round(t_ref_open, 1),
+                   "recall_sweep": rsweep,
                    "what": "the reference's own CUDA kernels (compiled from its sources) on this GPU; "
-                           "GustANNStats.run_time: nav + traversal, host translate included"}
+                           "GustANNStats.run_time: nav + traversal, host translate included; recall over the "
+                           "queries inside the reference's defined behaviour at each ef"}
+    with open(os.path.join(root, "reference_sweep.json"), "w") as f:
+        json.dump({"oracle": sweep, "reference_gpu": ref_gpu and ref_gpu["recall_sweep"], "ef": ef}, f)
     out = {"impl": "reference", "metric": METRIC, "value": v, "unit": "queries/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot_t / len(times),
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-           "data": "synthetic", "config": config_json(args, spec, ef, rec),
-           "cpu_baseline": {"value": v, "unit": "queries/s", "cores": cores, "kind": "port",
-                            "sample": f"{per_step} queries per step at ef_search={ef}"},
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic", "config": config_json(args, spec, ef, rec, passes),
+           "cpu_baseline": {"value": v, "unit": "queries/s", "cores": cores, "cpu_model": cpu_model(),
+                            "kind": "port", "sample": f"{per_step} queries per step at ef_search={ef}"},
            "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-           "reference_gpu": ref_gpu}
+           "recall_sweep": sweep, "oracle_load_s": round(t_open, 1), "reference_gpu": ref_gpu}
     print(json.dumps(out), flush=True)
 
 
-def config_json(args, spec, ef, rec):
-    return {"workload": f"{args.config}: {spec.n} x {spec.dim}-d {'uint8' if spec.dtype == 0 else 'float32'} "
-                        f"{spec.kind}-like mixture ({spec.centers} centers), R=64, PQ M=32, pivot graph, "
-                        f"{args.nq} queries/rank, top-{TOPK}",
-            "ef_search": ef, "recall_at_10": rec, "recall_target": args.target, "queries_per_rank": args.nq,
-            "l2_flush": "not needed: index (>6 GB) larger than L2",
-            "parallelism": f"query shards x{args.gpus}" + (f", records split x{args.gpus}"
-                                                            if getattr(args, "split_records", False) and args.gpus > 1
-                                                            else "")}
+def parity_report(args, o, root, Qs, nns, dist, found, ef):
+    """Outside the timed region: this arm's results against the oracle on the
+    first `parity_queries` queries, and against the reference's own kernels
+    (results the reference arm left in the cache) on every query they ran."""
+    n = min(args.parity_queries, len(Qs))
+    onns, odist, ofound, _, fl = o.search(Qs[:n], TOPK, ef, threads=os.cpu_count() or 1)
+    out = {"oracle": {"queries": n, "id_mismatches": int((onns != nns[:n]).any(1).sum()),
+                      "dist_mismatches": int((odist != dist[:n]).any(1).sum()),
+                      "found_mismatches": int((ofound != found[:n]).sum()),
+                      "undefined_behaviour_queries": int((fl != 0).sum())}}
+    p = os.path.join(root, f"refgpu_ef{ef}.npz")
+    if os.path.exists(p):
+        z = np.load(p)
+        idx = z["idx"]
+        idx_ok = idx < len(nns)
+        idx = idx[idx_ok]
+        out["reference_gpu"] = {"queries": int(len(idx)),
+                                "id_mismatches": int((z["nns"][idx_ok] != nns[idx]).any(1).sum()),
+                                "dist_mismatches": int((z["dist"][idx_ok] != dist[idx]).any(1).sum()),
+                                "found_mismatches": int((z["found"][idx_ok] != found[idx]).sum())}
+    return out
 
 
 def run_ours(args, d: Dist):
     from gustann_b200.api import GustANN, GustANNConfig, GustANNStats
     spec = spec_for(args)
-    paths = ensure_index(spec, args, d)
+    root = ensure_index(args, spec, d)
+    paths, Q, gt, meta = load_workload(root, spec)
+    passes = meta.get("passes", 2)
     dev = d.local
-    Q = datagen.as_float_queries(datagen.query_vectors(spec, args.nq, device="cuda", offset=d.rank))
-    gt = ground_truth(spec, Q)
+    lo, hi = shard(len(Q), d.rank, d.world)
+    Qs = np.ascontiguousarray(Q[lo:hi])
     g = GustANN(spec.dtype, device=dev)
     cfg = GustANNConfig(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"])
+    t0 = time.time()
     split = args.split_records and d.world > 1
     if split:
         from gustann_b200.sharding import exchange_parts
@@ -364,27 +463,28 @@ def run_ours(args, d: Dist):
         exchange_parts(g, d.rank, d.world)
     else:
         g.init_pure_mem(cfg, True)
+    t_open = time.time() - t0
 
+    # operating point: every rank sweeps the same first queries of the set, so
+    # all choose the same ef; the sweep covers every ef of the list
+    rq = min(len(Q), RECALL_QUERIES)
     efs = [int(x) for x in args.efs.split(",")]
-    sweep = []
-    ef, rec = efs[-1], 0.0
+    sweep, ef = [], None
     for e in efs:
-        nns, _, _ = g.query(Q, TOPK, e)
-        r = recall_at(nns, gt)
-        sweep.append((e, round(r, 4)))
-        if r >= args.target:
-            ef, rec = e, r
-            break
-        rec = r
-    # every rank must time the same ef: take the largest chosen one
-    ef = int(d.max(float(ef)))
+        nns, _, _ = g.query(Q[:rq], TOPK, e)
+        r = recall_at(nns, gt[:rq])
+        sweep.append((e, round(r, 5)))
+        if ef is None and r >= args.target:
+            ef = e
+    ef = int(d.max(float(ef if ef is not None else efs[-1])))
     st = GustANNStats()
-    nns, _, _ = g.query(Q, TOPK, ef, st)
-    rec = recall_at(nns, gt)
+    nns, dist, found = g.query(Qs, TOPK, ef, st)
     assert st.capped_queries == 0
+    hits = d.sum(float(recall_hits(nns, gt[lo:hi])))
+    rec = hits / (len(Q) * TOPK)
 
-    nq = len(Q)
-    dq = torch.from_numpy(Q).cuda(dev)
+    nq = len(Qs)
+    dq = torch.from_numpy(Qs).cuda(dev)
     dn = torch.empty((nq, TOPK), dtype=torch.int32, device=dev)
     dd = torch.empty((nq, TOPK), dtype=torch.float32, device=dev)
     df = torch.empty(nq, dtype=torch.int32, device=dev)
@@ -414,12 +514,13 @@ def run_ours(args, d: Dist):
     d.barrier()
     ck = clocks.stop(t_begin, t_end)
     step_ms = [a.elapsed_time(b) for a, b in evs]
+    same = bool(torch.equal(dn.cpu(), torch.from_numpy(nns)))
     t_step = d.max(float(np.mean(step_ms)))
     total_q = d.sum(float(nq))
     value = total_q / (t_step * 1e-3)
 
     # e2e: the reference-facing call with host buffers (pinned), copies included
-    hq = torch.from_numpy(Q).pin_memory().numpy()
+    hq = torch.from_numpy(Qs).pin_memory().numpy()
     hn = torch.zeros((nq, TOPK), dtype=torch.int32).pin_memory().numpy()
     hd = torch.zeros((nq, TOPK), dtype=torch.float32).pin_memory().numpy()
     hf = torch.zeros(nq, dtype=torch.int32).pin_memory().numpy()
@@ -433,7 +534,7 @@ def run_ours(args, d: Dist):
     t_e2e = (time.perf_counter() - t0) / args.steps
     d.barrier()
     t_e2e = d.max(t_e2e)
-    e2e = {"value": total_q / t_e2e, "unit": "queries/s", "h2d_bytes_per_step": int(Q.nbytes),
+    e2e = {"value": total_q / t_e2e, "unit": "queries/s", "h2d_bytes_per_step": int(Qs.nbytes),
            "d2h_bytes_per_step": int(hn.nbytes + hd.nbytes + hf.nbytes)}
 
     peak, peak_kind = measured_peak()
@@ -447,18 +548,44 @@ def run_ours(args, d: Dist):
 
     out = None
     if d.rank == 0:
-        cpu = None
+        cpu = parity = None
         if d.world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(paths, spec.dtype, Q, ef, args.cpu_seconds)
+            orc = oracle_module()
+            o = orc.Oracle(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], spec.dtype)
+            parity = parity_report(args, o, root, Qs, nns, dist, found, ef)
+            cpu = cpu_baseline(o, Qs[:rq], ef, args.cpu_seconds)
+            o.close()
+        ref_sweep = None
+        p = os.path.join(root, "reference_sweep.json")
+        if os.path.exists(p):
+            with open(p) as f:
+                ref_sweep = json.load(f)
+        table = recall_table(sweep, ref_sweep)
         out = {"metric": METRIC, "value": round(value, 1), "unit": "queries/s", "n_gpus": d.world,
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_step, 4),
-               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-               "data": "synthetic", "config": config_json(args, spec, ef, rec), "e2e": e2e,
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+               "data": "synthetic", "config": config_json(args, spec, ef, round(rec, 5), passes), "e2e": e2e,
                "roofline": roof, "cpu_baseline": cpu, "clocks": ck, "gpu_launches": args.steps,
-               "recall_sweep": sweep}
+               "parity": parity, "timed_results_equal_untimed": same, "recall_sweep": table,
+               "index_build_s": meta.get("timings"), "index_load_s": round(t_open, 1)}
     d.barrier()          # split records: peers read this rank's range until every rank is done
     g.close()
     return out
+
+
+def recall_table(sweep, ref_sweep):
+    """Recall@10 on the first queries of the set at every swept ef: this arm,
+    the oracle and the reference's own kernels (the latter two from the
+    reference arm's run, when it left them in the cache), and the largest
+    |difference| to each."""
+    ora = dict(map(tuple, ref_sweep["oracle"])) if ref_sweep else {}
+    rg = {e: r for e, r, _ in (ref_sweep.get("reference_gpu") or [])} if ref_sweep else {}
+    rows = [{"ef": e, "ours": r, "oracle": ora.get(e), "reference_gpu": rg.get(e)} for e, r in sweep]
+    d_o = [abs(x["ours"] - x["oracle"]) for x in rows if x["oracle"] is not None]
+    d_r = [abs(x["ours"] - x["reference_gpu"]) for x in rows if x["reference_gpu"] is not None]
+    return {"rows": rows, "max_abs_diff_oracle": max(d_o) if d_o else None,
+            "max_abs_diff_reference_gpu": max(d_r) if d_r else None,
+            "note": "reference_gpu recall is over the queries inside the reference's defined behaviour at that ef"}
 
 
 def main():

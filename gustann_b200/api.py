@@ -29,10 +29,12 @@ STATUS_NAMES = ["OK", "EINVAL", "EIO", "ENOMEM", "ECUDA", "ETIMEDOUT", "EUNSUPPO
 EXPORTS = ["gann_open", "gann_open_device", "gann_search", "gann_search_device", "gann_close", "gann_last_error",
            "gann_index_info", "gann_probe_lut", "gann_probe_entry", "gann_pivot_sample", "gann_set_option",
            "gann_search_noalloc", "gann_part_export", "gann_part_attach", "gann_hop_begin", "gann_hop_requests",
-           "gann_hop_step", "gann_hop_finish", "gann_hop_free", "gann_read_pages"]
+           "gann_hop_step", "gann_hop_finish", "gann_hop_free", "gann_read_pages", "gann_exact_knn",
+           "gann_robust_prune", "gann_sort_unique_rows"]
 GANN_OPT_ADC_MODE, GANN_OPT_PIVOT_WARPS, GANN_OPT_NEIGHBOUR_CODES = 1, 2, 3
 LAYOUT_AUTO, LAYOUT_SEPARATE, LAYOUT_NEIGHBOUR_CODES = 0, 1, 2
 ADC_AUTO, ADC_TABLE, ADC_PIVOT = 0, 1, 2
+METRIC_L2, METRIC_IP = 0, 1
 
 
 class GustANNError(RuntimeError):
@@ -46,7 +48,7 @@ class _Config(C.Structure):
     _fields_ = [("index_file", C.c_char_p), ("pq_file_prefix", C.c_char_p), ("nav_graph_prefix", C.c_char_p),
                 ("dtype", C.c_int32), ("use_gpu_mem", C.c_int32), ("device", C.c_int32),
                 ("layout", C.c_int32), ("part_count", C.c_int32), ("part_index", C.c_int32),
-                ("reserved", C.c_int32 * 2)]
+                ("metric", C.c_int32), ("reserved", C.c_int32 * 1)]
 
 
 class _Stats(C.Structure):
@@ -60,7 +62,7 @@ class _DeviceIndex(C.Structure):
                 ("code_stride", C.c_int32), ("pq_chunks", C.c_int32), ("pivots", C.c_void_p),
                 ("centroid", C.c_void_p), ("chunk_offsets", C.c_void_p), ("num_points", C.c_int64),
                 ("dim", C.c_int32), ("dtype", C.c_int32), ("medoid", C.c_int64), ("device", C.c_int32),
-                ("reserved", C.c_int32 * 3)]
+                ("metric", C.c_int32), ("reserved", C.c_int32 * 2)]
 
 
 class _Info(C.Structure):
@@ -95,6 +97,9 @@ def _load() -> C.CDLL:
     lib.gann_hop_finish.argtypes = [vp, ip, fp, ip]
     lib.gann_hop_free.argtypes = [vp]
     lib.gann_read_pages.argtypes = [C.c_char_p, ip, i64, i32, vp, i32]
+    lib.gann_exact_knn.argtypes = [vp, i64, i64, i32, i32, vp, i64, i64, i32, i32, vp, vp, i32, vp]
+    lib.gann_robust_prune.argtypes = [vp, i64, i64, i32, i32, vp, i64, vp, vp, i32, i32, C.c_float, vp, vp, i32, vp]
+    lib.gann_sort_unique_rows.argtypes = [vp, vp, i64, i32, vp, vp, i32, vp]
     for name in EXPORTS:
         if name != "gann_last_error":
             getattr(lib, name).restype = C.c_int
@@ -135,14 +140,17 @@ class GustANNStats:
 
 
 class GustANN:
-    """Drop-in for ``gustann::GustANN`` on one B200 (``device``)."""
+    """Drop-in for ``gustann::GustANN`` on one B200 (``device``). ``metric``
+    (an extension; the reference is L2-only) is :data:`METRIC_L2` or
+    :data:`METRIC_IP` (distances -<q, x>)."""
 
-    def __init__(self, data_type: int = FLOAT, device: int = 0, layout: int = 0):
+    def __init__(self, data_type: int = FLOAT, device: int = 0, layout: int = 0, metric: int = METRIC_L2):
         if data_type not in (UINT8, FLOAT):
             raise GustANNError(GANN_EINVAL, "data type must be UINT8 (0) or FLOAT (1)")
         self.data_type = data_type
         self.device = device
         self.layout = layout
+        self.metric = metric
         self._h = None
         self.dim = 0
 
@@ -156,7 +164,7 @@ class GustANN:
         self.close()
         cfg = _Config(config.index_file.encode(), config.pq_file_prefix.encode(),
                       (config.nav_graph_prefix or "").encode(), self.data_type, int(bool(use_gpu_mem)),
-                      self.device, self.layout, part_count, part_index)
+                      self.device, self.layout, part_count, part_index, self.metric)
         h = C.c_void_p()
         _check(lib.gann_open(C.byref(cfg), C.byref(h)))
         self._h = h
@@ -164,29 +172,27 @@ class GustANN:
 
     @classmethod
     def from_device(cls, vectors, adjacency, codes, pivots: np.ndarray, centroid: np.ndarray,
-                    chunk_offsets: np.ndarray, medoid: int, max_degree: int, device: int = 0) -> "GustANN":
+                    chunk_offsets: np.ndarray, medoid: int, max_degree: int, device: int = 0,
+                    metric: int = METRIC_L2) -> "GustANN":
         """Search over caller-owned CUDA tensors (``gann_open_device``): ``vectors``
         [n, d] uint8/float32, ``adjacency`` [n, stride] int32 (-1 = empty slot),
         ``codes`` [n, code_stride] uint8. The tensors must stay alive and may be
         rewritten between searches."""
         dt = UINT8 if vectors.dtype.itemsize == 1 else FLOAT
-        g = cls(dt, device)
+        g = cls(dt, device, metric=metric)
         piv = np.ascontiguousarray(pivots, np.float32)
         cen = np.ascontiguousarray(centroid, np.float32)
         off = np.ascontiguousarray(chunk_offsets, np.uint32)
         d = _DeviceIndex(vectors.data_ptr(), vectors.stride(0) * vectors.element_size(), adjacency.data_ptr(),
                          adjacency.stride(0), max_degree, codes.data_ptr(), codes.stride(0), len(off) - 1,
-                         _ptr(piv), _ptr(cen), _ptr(off), vectors.shape[0], vectors.shape[1], dt, medoid, device)
+                         _ptr(piv), _ptr(cen), _ptr(off), vectors.shape[0], vectors.shape[1], dt, medoid, device,
+                         metric)
         h = C.c_void_p()
         _check(lib.gann_open_device(C.byref(d), C.byref(h)))
         g._h = h
         g.dim = int(vectors.shape[1])
         g._keep = (vectors, adjacency, codes)
         return g
-
-    def init_hybrid(self, *args, **kwargs) -> None:
-        """The SSD-tiered executor is not part of this build."""
-        raise GustANNError(GANN_EUNSUPPORTED, "init_hybrid: SSD-hybrid search is not provided by this build")
 
     def init_bam(self, *args, **kwargs) -> None:
         raise GustANNError(GANN_EUNSUPPORTED, "init_bam: BaM search is not provided by this build")
@@ -270,7 +276,8 @@ class GustANN:
         ``mini_batch`` and ``thread_cnt`` (``HybridExecutorConfig``)."""
         self.close()
         cfg = _Config(config.index_file.encode(), config.pq_file_prefix.encode(),
-                      (config.nav_graph_prefix or "").encode(), self.data_type, 2, self.device, 1, 0, 0)
+                      (config.nav_graph_prefix or "").encode(), self.data_type, 2, self.device, 1, 0, 0,
+                      self.metric)
         h = C.c_void_p()
         _check(lib.gann_open(C.byref(cfg), C.byref(h)))
         self._h = h
@@ -363,6 +370,68 @@ class GustANN:
 
     def __exit__(self, *exc):
         self.close()
+
+
+def exact_knn(base, queries, k: int, metric: int = METRIC_L2, stream: int = 0):
+    """Exact ``k`` nearest rows of ``base`` for every row of ``queries``
+    (``gann_exact_knn``): CUDA tensors of one dtype (uint8 or float32), rows
+    16-byte aligned. Returns ``(ids int32 [nq, k], dists float32 [nq, k])`` on
+    the same device, ascending by (distance, id); L2 distances are squared."""
+    import torch
+    if base.dtype != queries.dtype or base.dtype not in (torch.uint8, torch.float32):
+        raise GustANNError(GANN_EINVAL, "exact_knn: base and queries must both be uint8 or float32")
+    if not (base.is_cuda and queries.is_cuda) or base.device != queries.device:
+        raise GustANNError(GANN_EINVAL, "exact_knn: tensors must be on one CUDA device")
+    if base.stride(1) != 1 or queries.stride(1) != 1:
+        raise GustANNError(GANN_EINVAL, "exact_knn: rows must be contiguous")
+    dt = UINT8 if base.dtype == torch.uint8 else FLOAT
+    nq = queries.shape[0]
+    ids = torch.empty((nq, k), dtype=torch.int32, device=base.device)
+    dists = torch.empty((nq, k), dtype=torch.float32, device=base.device)
+    es = base.element_size()
+    _check(lib.gann_exact_knn(base.data_ptr(), base.shape[0], base.stride(0) * es, base.shape[1], dt,
+                              queries.data_ptr(), queries.stride(0) * es, nq, k, metric, ids.data_ptr(),
+                              dists.data_ptr(), base.device.index or 0, stream or None))
+    return ids, dists
+
+
+def robust_prune(vectors, points, cand, cand_dist, r: int, alpha: float, stream: int = 0):
+    """RobustPrune of many points on the GPU (``gann_robust_prune``):
+    ``vectors`` [n, d] uint8/float32 CUDA tensor (rows 16-byte aligned),
+    ``points`` [b] int32, ``cand`` [b, k] int32 candidates nearest-first (-1
+    empty), ``cand_dist`` [b, k] float32 squared distances to the point.
+    Returns (kept [b, r] int32 nearest-first, -1 padded; their distances)."""
+    import torch
+    if vectors.dtype not in (torch.uint8, torch.float32) or vectors.stride(1) != 1:
+        raise GustANNError(GANN_EINVAL, "robust_prune: vectors must be uint8/float32 with contiguous rows")
+    dt = UINT8 if vectors.dtype == torch.uint8 else FLOAT
+    pts = points.to(torch.int32).contiguous()
+    ci = cand.to(torch.int32).contiguous()
+    cd = cand_dist.to(torch.float32).contiguous()
+    b, k = ci.shape
+    out = torch.empty((b, r), dtype=torch.int32, device=vectors.device)
+    outd = torch.empty((b, r), dtype=torch.float32, device=vectors.device)
+    _check(lib.gann_robust_prune(vectors.data_ptr(), vectors.shape[0], vectors.stride(0) * vectors.element_size(),
+                                 vectors.shape[1], dt, pts.data_ptr(), b, ci.data_ptr(), cd.data_ptr(), k, r,
+                                 float(alpha), out.data_ptr(), outd.data_ptr(), vectors.device.index or 0,
+                                 stream or None))
+    return out, outd
+
+
+def sort_unique_rows(ids, dists, stream: int = 0):
+    """Rows of (id, distance) candidates sorted by (distance, id) with empty
+    slots (id < 0) and repeated ids removed, -1/+inf padded
+    (``gann_sort_unique_rows``). CUDA tensors [rows, k], k <= 256; returns
+    (ids int32, dists float32) of the same shape."""
+    import torch
+    i = ids.to(torch.int32).contiguous()
+    d = dists.to(torch.float32).contiguous()
+    rows, k = i.shape
+    oi = torch.empty_like(i)
+    od = torch.empty_like(d)
+    _check(lib.gann_sort_unique_rows(i.data_ptr(), d.data_ptr(), rows, k, oi.data_ptr(), od.data_ptr(),
+                                     i.device.index or 0, stream or None))
+    return oi, od
 
 
 def pivot_sample(n: int, s: int, seed: int = 114514) -> np.ndarray:

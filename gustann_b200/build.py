@@ -3,6 +3,7 @@
 Outputs (git-ignored, shipped with the tree):
   gustann_b200/_lib/libgann.so   C ABI of include/gann.h
   gustann_b200/_lib/search_mem   CLI with the reference driver's flags
+  gustann_b200/_lib/check_recall recall of a result file against an ivecs ground truth
 
 Run ``python -m gustann_b200.build`` (idempotent; rebuilds when a source is newer).
 """
@@ -21,8 +22,9 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIB = os.path.join(OUT, "libgann.so")
 CLI = os.path.join(OUT, "search_mem")
+CHECK = os.path.join(OUT, "check_recall")
 
-LIB_SOURCES = ["gann_search.cu", "gann_api.cu", "gann_loader.cpp"]
+LIB_SOURCES = ["gann_search.cu", "gann_api.cu", "gann_loader.cpp", "gann_exact.cu", "gann_build.cu"]
 HEADERS = ["gann_internal.hpp"]
 
 
@@ -62,9 +64,18 @@ def build_cli(force: bool = False) -> str:
     return CLI
 
 
+def build_check(force: bool = False) -> str:
+    src = os.path.join(CSRC, "check_recall.cpp")
+    if force or _newer(CHECK, [src]):
+        _run(["g++", "-O2", "-std=c++17", src, "-o", CHECK + ".tmp"])
+        os.replace(CHECK + ".tmp", CHECK)
+    return CHECK
+
+
 def build_all(force: bool = False) -> None:
     build_lib(force)
     build_cli(force)
+    build_check(force)
 
 
 if __name__ == "__main__":

@@ -293,6 +293,8 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
   h->host_records = cfg->use_gpu_mem == 0;
   h->storage_records = cfg->use_gpu_mem == 2;
   if (cfg->layout < 0 || cfg->layout > 2) return set_error(GANN_EINVAL, "gann_open: layout must be 0, 1 or 2");
+  if (cfg->metric != GANN_METRIC_L2 && cfg->metric != GANN_METRIC_IP)
+    return set_error(GANN_EINVAL, "gann_open: metric must be GANN_METRIC_L2 or GANN_METRIC_IP");
   if (cfg->part_count < 0 || cfg->part_count > gann::kMaxParts)
     return set_error(GANN_EINVAL, "gann_open: part_count must be 0..8");
   h->part_count = cfg->part_count > 1 ? cfg->part_count : 0;
@@ -329,6 +331,7 @@ int open_impl(const gann_config* cfg, gann_handle* h) {
   GANN_CUDA(cudaEventCreate(&h->ev1));
 
   DeviceIndex& ix = h->ix;
+  ix.metric = cfg->metric;
   ix.n = hi.num_points;
   ix.dim = static_cast<int32_t>(hi.dim);
   ix.degree = static_cast<int32_t>(hi.max_m0);
@@ -449,6 +452,8 @@ int open_device_impl(const gann_device_index* d, gann_handle* h) {
       d->pq_chunks > 128 || d->code_stride < d->pq_chunks || d->adj_stride % 4)
     return set_error(GANN_EINVAL, "gann_open_device: bad row strides");
   if (d->medoid < 0 || d->medoid >= d->num_points) return set_error(GANN_EINVAL, "gann_open_device: bad medoid");
+  if (d->metric != GANN_METRIC_L2 && d->metric != GANN_METRIC_IP)
+    return set_error(GANN_EINVAL, "gann_open_device: bad metric");
   const uint32_t* off = d->chunk_offsets;
   if (off[0] != 0 || off[d->pq_chunks] != static_cast<uint32_t>(d->dim))
     return set_error(GANN_EINVAL, "gann_open_device: chunk offsets must span [0, dim]");
@@ -503,6 +508,7 @@ int open_device_impl(const gann_device_index* d, gann_handle* h) {
   ix.adj_stride = d->adj_stride;
   ix.code_stride = d->code_stride;
   ix.medoid = d->medoid;
+  ix.metric = d->metric;
   ix.has_nav = 0;
   return upload_pivot_table(h);
 }
@@ -993,6 +999,93 @@ int gann_pivot_sample(int64_t n, int64_t s, uint32_t seed, int32_t* out) {
   return GANN_OK;
 }
 
+int gann_exact_knn(const void* d_base, int64_t num_points, int64_t base_stride, int32_t dim, int32_t dtype,
+                   const void* d_queries, int64_t query_stride, int64_t nq, int32_t k, int32_t metric,
+                   int32_t* d_ids, float* d_distances, int32_t device, void* stream) {
+  if (dtype != GANN_UINT8 && dtype != GANN_FLOAT) return set_error(GANN_EINVAL, "gann_exact_knn: bad dtype");
+  if (metric != GANN_METRIC_L2 && metric != GANN_METRIC_IP) return set_error(GANN_EINVAL, "gann_exact_knn: bad metric");
+  const int64_t elem = dtype == GANN_UINT8 ? 1 : 4;
+  if (num_points <= 0 || num_points >= (int64_t(1) << 31) || dim <= 0 || dim > 4096 || nq < 0)
+    return set_error(GANN_EINVAL, "gann_exact_knn: bad size");
+  if (k < 1 || k > gann::exact_knn_max_k() || k > num_points)
+    return set_error(GANN_EINVAL, "gann_exact_knn: need 1 <= k <= min(128, num_points)");
+  if (base_stride < dim * elem || query_stride < dim * elem || base_stride % 16 || query_stride % 16)
+    return set_error(GANN_EINVAL, "gann_exact_knn: strides must cover a row and be multiples of 16 bytes");
+  if (nq == 0) return GANN_OK;
+  if (!d_base || !d_queries || !d_ids || !d_distances || reinterpret_cast<uintptr_t>(d_base) % 16 ||
+      reinterpret_cast<uintptr_t>(d_queries) % 16)
+    return set_error(GANN_EINVAL, "gann_exact_knn: null or unaligned buffer");
+  int ndev = 0;
+  GANN_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return set_error(GANN_EINVAL, "gann_exact_knn: no such CUDA device");
+  int prev = 0;
+  GANN_CUDA(cudaGetDevice(&prev));
+  GANN_CUDA(cudaSetDevice(device));
+  int sm = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess)
+    e = gann::launch_exact_knn(d_base, num_points, base_stride, dim, dtype, d_queries, query_stride, nq, k, metric,
+                               d_ids, d_distances, sm, static_cast<cudaStream_t>(stream));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess)
+    return set_error(e == cudaErrorMemoryAllocation ? GANN_ENOMEM : GANN_ECUDA,
+                     std::string("gann_exact_knn: ") + cudaGetErrorString(e));
+  return GANN_OK;
+}
+
+int gann_robust_prune(const void* d_vectors, int64_t num_points, int64_t stride, int32_t dim, int32_t dtype,
+                      const int32_t* d_points, int64_t count, const int32_t* d_cand, const float* d_cand_dist,
+                      int32_t k, int32_t r, float alpha, int32_t* d_out, float* d_out_dist, int32_t device,
+                      void* stream) {
+  if (dtype != GANN_UINT8 && dtype != GANN_FLOAT) return set_error(GANN_EINVAL, "gann_robust_prune: bad dtype");
+  const int64_t elem = dtype == GANN_UINT8 ? 1 : 4;
+  if (num_points <= 0 || num_points >= (int64_t(1) << 31) || dim <= 0 || dim > 4096 || count < 0)
+    return set_error(GANN_EINVAL, "gann_robust_prune: bad size");
+  if (k < 1 || k > gann::prune_max_candidates() || r < 1 || !(alpha >= 1.f))
+    return set_error(GANN_EINVAL, "gann_robust_prune: need 1 <= k <= 256, r >= 1, alpha >= 1");
+  if (stride < dim * elem || stride % 16 || reinterpret_cast<uintptr_t>(d_vectors) % 16)
+    return set_error(GANN_EINVAL, "gann_robust_prune: vector rows must be 16-byte aligned");
+  if (count == 0) return GANN_OK;
+  if (!d_vectors || !d_points || !d_cand || !d_cand_dist || !d_out || !d_out_dist)
+    return set_error(GANN_EINVAL, "gann_robust_prune: null buffer");
+  int ndev = 0;
+  GANN_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return set_error(GANN_EINVAL, "gann_robust_prune: no such CUDA device");
+  int prev = 0;
+  GANN_CUDA(cudaGetDevice(&prev));
+  GANN_CUDA(cudaSetDevice(device));
+  int sm = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess)
+    e = gann::launch_robust_prune(d_vectors, num_points, stride, dim, dtype, d_points, count, d_cand, d_cand_dist,
+                                  k, r, alpha, d_out, d_out_dist, sm, static_cast<cudaStream_t>(stream));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return set_error(GANN_ECUDA, std::string("gann_robust_prune: ") + cudaGetErrorString(e));
+  return GANN_OK;
+}
+
+int gann_sort_unique_rows(const int32_t* d_ids, const float* d_dists, int64_t rows, int32_t k, int32_t* d_out_ids,
+                          float* d_out_dists, int32_t device, void* stream) {
+  if (rows < 0 || k < 1 || k > gann::prune_max_candidates())
+    return set_error(GANN_EINVAL, "gann_sort_unique_rows: need rows >= 0 and 1 <= k <= 256");
+  if (rows == 0) return GANN_OK;
+  if (!d_ids || !d_dists || !d_out_ids || !d_out_dists) return set_error(GANN_EINVAL, "gann_sort_unique_rows: null buffer");
+  int ndev = 0;
+  GANN_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return set_error(GANN_EINVAL, "gann_sort_unique_rows: no such CUDA device");
+  int prev = 0;
+  GANN_CUDA(cudaGetDevice(&prev));
+  GANN_CUDA(cudaSetDevice(device));
+  int sm = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess)
+    e = gann::launch_sort_unique_rows(d_ids, d_dists, rows, k, d_out_ids, d_out_dists, sm,
+                                      static_cast<cudaStream_t>(stream));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return set_error(GANN_ECUDA, std::string("gann_sort_unique_rows: ") + cudaGetErrorString(e));
+  return GANN_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
@@ -1051,6 +1144,8 @@ extern "C" int gann_search_noalloc(const gann_device_index* d, const float* d_qu
       d->pq_chunks > 128 || d->code_stride < d->pq_chunks)
     return set_error(GANN_EINVAL, "gann_search_noalloc: bad row strides");
   if (d->medoid < 0 || d->medoid >= d->num_points) return set_error(GANN_EINVAL, "gann_search_noalloc: bad medoid");
+  if (d->metric != GANN_METRIC_L2 && d->metric != GANN_METRIC_IP)
+    return set_error(GANN_EINVAL, "gann_search_noalloc: bad metric");
   const uint32_t* off = d->chunk_offsets;
   const int m = d->pq_chunks, dim = d->dim;
   if (off[0] != 0 || off[m] != static_cast<uint32_t>(dim))
@@ -1090,7 +1185,11 @@ extern "C" int gann_search_noalloc(const gann_device_index* d, const float* d_qu
 
   if (d->device < 0 || d->device >= kNoallocMaxDevices)
     return set_error(GANN_EUNSUPPORTED, "gann_search_noalloc: device ordinal outside 0..63");
+  // the caller's current device is restored on every return path
+  int prev_dev = 0;
+  GANN_CUDA(cudaGetDevice(&prev_dev));
   GANN_CUDA(cudaSetDevice(d->device));
+  auto on_device = [&]() -> int {
   unsigned char* base = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
@@ -1131,6 +1230,7 @@ extern "C" int gann_search_noalloc(const gann_device_index* d, const float* d_qu
   ix.adj_stride = d->adj_stride;
   ix.code_stride = d->code_stride;
   ix.medoid = d->medoid;
+  ix.metric = d->metric;
   ix.has_nav = 0;
   ix.piv4 = piv_width ? reinterpret_cast<const float4*>(base + o_piv) : nullptr;
   ix.piv_width = piv_width;
@@ -1154,4 +1254,8 @@ extern "C" int gann_search_noalloc(const gann_device_index* d, const float* d_qu
   a.err = reinterpret_cast<int32_t*>(base) + 1;
   GANN_CUDA(gann::launch_search(ix, a, d->dtype, sm_count, st));
   return GANN_OK;
+  };
+  const int rc = on_device();
+  cudaSetDevice(prev_dev);
+  return rc;
 }

@@ -72,6 +72,7 @@ struct DeviceIndex {
   // each code_stride bytes (nullptr when the index keeps codes separate only)
   const uint8_t* ncodes = nullptr;
   int32_t adc_mode = 0;     // 0 auto, 1 table, 2 pivot
+  int32_t metric = 0;       // GANN_METRIC_L2 / GANN_METRIC_IP
   int32_t piv_warps = 0;    // 0 = as many as fit (<= 24)
   // records split by id (nparts > 1): part p holds ids [p << part_shift,
   // (p + 1) << part_shift) in its own arrays (possibly another GPU's memory,
@@ -145,6 +146,18 @@ size_t search_smem_bytes(const DeviceIndex& ix, int topk, int ef);
 int make_pivot_table(const std::vector<float>& pivots_t, const std::vector<int32_t>& chunk_off, int dim,
                      std::vector<float>& out);
 int search_max_ef();
+// RobustPrune for the GPU index builder (gann_build.cu).
+int prune_max_candidates();
+cudaError_t launch_sort_unique_rows(const int32_t* ids, const float* dists, int64_t rows, int k, int32_t* out_ids,
+                                    float* out_d, int sm_count, cudaStream_t st);
+cudaError_t launch_robust_prune(const void* vecs, int64_t n, int64_t stride, int dim, int dtype,
+                                const int32_t* points, int64_t b, const int32_t* cand, const float* cdist, int k,
+                                int r, float alpha, int32_t* out, float* outd, int sm_count, cudaStream_t st);
+// Exact brute-force k-NN (gann_exact.cu).
+int exact_knn_max_k();
+cudaError_t launch_exact_knn(const void* base, int64_t n, int64_t bstride, int dim, int dtype, const void* queries,
+                             int64_t qstride, int64_t nq, int k, int metric, int32_t* ids, float* dists,
+                             int sm_count, cudaStream_t st);
 cudaError_t launch_gather_neighbour_codes(const uint32_t* adj, int adj_stride, int degree, const uint8_t* codes,
                                           int code_stride, int64_t n, uint8_t* out, cudaStream_t st);
 

@@ -13,6 +13,10 @@
 //   * exact distance: lane-strided fma partial sums, then the shfl_down tree
 //     16/8/4/2/1 (src/impl/util.cuh:26-46), on q'' = (q - c) + c for the
 //     traversal re-rank and on q for the pivot graph.
+// With the inner-product metric (no counterpart in the reference, which is
+// L2-only: src/common.hpp:28-30) every distance is -<q, x>: table entries
+// -(fma chain of q_i * p_ji from 0 over the chunk's dims), exact distances the
+// same lane-strided fma sums and shfl_down tree on q . x, negated; q'' = q.
 // Candidate order is the total order (distance, id & 0x7fffffff)
 // (src/impl/util.cuh:166-178); the pool keeps the first `ef` distinct entries
 // of merge(pool, neighbours) with the pool copy first on equal keys, which is
@@ -65,28 +69,35 @@ __device__ __forceinline__ void load32<float>(const float* __restrict__ p, float
   }
 }
 
-// Exact squared L2 with the reference's warp order: lane l sums dims l, l+32, ...
-// with fma, then the shfl_down tree (src/impl/util.cuh:26-46). All lanes get
-// lane 0's value.
-template <typename T>
-__device__ __forceinline__ float warp_sqdist(const float* __restrict__ qv, const T* __restrict__ x,
-                                             int dim, int lane) {
+// One lane's term of an exact distance: squared difference, or the product
+// for the inner product.
+template <bool IP>
+__device__ __forceinline__ float dist_acc(float q, float x, float acc) {
+  if (IP) return __fmaf_rn(q, x, acc);
+  const float d = __fsub_rn(q, x);
+  return __fmaf_rn(d, d, acc);
+}
+
+// Exact distance with the reference's warp order: lane l sums dims l, l+32, ...
+// with fma, then the shfl_down tree (src/impl/util.cuh:26-46); negated for the
+// inner product. All lanes get lane 0's value.
+template <typename T, bool IP>
+__device__ __forceinline__ float warp_dist(const float* __restrict__ qv, const T* __restrict__ x,
+                                           int dim, int lane) {
   float acc = 0.f;
-  for (int i = lane; i < dim; i += kWarp) {
-    float d = __fsub_rn(qv[i], static_cast<float>(x[i]));
-    acc = __fmaf_rn(d, d, acc);
-  }
+  for (int i = lane; i < dim; i += kWarp) acc = dist_acc<IP>(qv[i], static_cast<float>(x[i]), acc);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, off));
-  return __shfl_sync(kFull, acc, 0);
+  const float r = __shfl_sync(kFull, acc, 0);
+  return IP ? -r : r;
 }
 
 // The same value computed by ONE lane for a whole vector: the 32 lane partials
 // live in registers and the shfl_down tree is replayed (lane 0's sum at every
 // level), so 28 pivot-graph neighbours are measured at once, one per lane.
-template <typename T>
-__device__ __forceinline__ float lane_sqdist(const float* __restrict__ qv, const T* __restrict__ x,
-                                             int dim) {
+template <typename T, bool IP>
+__device__ __forceinline__ float lane_dist(const float* __restrict__ qv, const T* __restrict__ x,
+                                           int dim) {
   float p[32];
 #pragma unroll
   for (int m = 0; m < 32; ++m) p[m] = 0.f;
@@ -95,10 +106,7 @@ __device__ __forceinline__ float lane_sqdist(const float* __restrict__ qv, const
     load32<T>(x + base, xv);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
-      if (base + m < dim) {
-        float d = __fsub_rn(qv[base + m], xv[m]);
-        p[m] = __fmaf_rn(d, d, p[m]);
-      }
+      if (base + m < dim) p[m] = dist_acc<IP>(qv[base + m], xv[m], p[m]);
     }
   }
 #pragma unroll
@@ -106,20 +114,20 @@ __device__ __forceinline__ float lane_sqdist(const float* __restrict__ qv, const
 #pragma unroll
     for (int m = 0; m < off; ++m) p[m] = __fadd_rn(p[m], p[m + off]);
   }
-  return p[0];
+  return IP ? -p[0] : p[0];
 }
 
 // Greedy entry search on the pivot graph (src/impl/nav.cuh:13-135), lane = slot.
 // Slots [0,4) hold the best entries, [4,32) the neighbours of the last expanded
 // node; slots past the neighbour count keep stale entries, as in the reference.
 // Returns the sample index of slot 0.
-template <typename T>
+template <typename T, bool IP>
 __device__ int nav_search(const DeviceIndex& ix, const float* __restrict__ qs, int lane,
                           int max_hops, bool& capped) {
   const T* nv = reinterpret_cast<const T*>(ix.nav_vecs);
   const size_t rs = static_cast<size_t>(ix.nav_stride) / sizeof(T);
   const int start = ix.nav_start;
-  const float d0 = warp_sqdist<T>(qs, nv + static_cast<size_t>(start) * rs, ix.dim, lane);
+  const float d0 = warp_dist<T, IP>(qs, nv + static_cast<size_t>(start) * rs, ix.dim, lane);
   uint32_t sid = lane == 0 ? static_cast<uint32_t>(start) : kPadId;
   float sd = lane == 0 ? d0 : INFINITY;
   int idx = 0;
@@ -135,7 +143,7 @@ __device__ int nav_search(const DeviceIndex& ix, const float* __restrict__ qs, i
     const unsigned term = __ballot_sync(kFull, lane >= kNavNbr || v == -1);
     const int cnt = __ffs(term) - 1;
     float dv = INFINITY;
-    if (lane < cnt) dv = lane_sqdist<T>(qs, nv + static_cast<size_t>(v) * rs, ix.dim);
+    if (lane < cnt) dv = lane_dist<T, IP>(qs, nv + static_cast<size_t>(v) * rs, ix.dim);
     const int src = lane >= kNavBest ? lane - kNavBest : 0;
     const uint32_t nid = __shfl_sync(kFull, static_cast<uint32_t>(v), src);
     const float nd = __shfl_sync(kFull, dv, src);
@@ -193,7 +201,9 @@ __device__ int nav_search(const DeviceIndex& ix, const float* __restrict__ qs, i
 }
 
 // ADC table of one query into `lut` [M x 256] (shared or global memory).
-// Lane l owns pivots 8l..8l+7 (two float4 loads per dimension).
+// Lane l owns pivots 8l..8l+7 (two float4 loads per dimension). `qc` is q - c
+// for L2 and q for the inner product.
+template <bool IP>
 __device__ __forceinline__ void build_lut(const DeviceIndex& ix, const float* __restrict__ qc,
                                           float* __restrict__ lut, int lane) {
   for (int c = 0; c < ix.chunks; ++c) {
@@ -207,10 +217,11 @@ __device__ __forceinline__ void build_lut(const DeviceIndex& ix, const float* __
       const float4 p0 = __ldg(p), p1 = __ldg(p + 1);
       const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float d = __fsub_rn(qi, pv[k]);
-        acc[k] = __fmaf_rn(d, d, acc[k]);
-      }
+      for (int k = 0; k < 8; ++k) acc[k] = dist_acc<IP>(qi, pv[k], acc[k]);
+    }
+    if (IP) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = -acc[k];
     }
     float4* o = reinterpret_cast<float4*>(lut + c * kPivots) + 2 * lane;
     o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
@@ -251,7 +262,7 @@ __host__ __device__ inline size_t piv_tab_bytes(int cw, int chunks) {
 // the reference's table entry, so the sum is bit-identical. CW = dims per
 // chunk (4 also serves mixed widths <= 4: the zero padding contributes
 // fma(0, 0, e) = e). `row0` is the first row of this 16-chunk group.
-template <int CW>
+template <int CW, bool IP>
 __device__ __forceinline__ float adc16_piv(float s, const uint4 c, const PivTab& t, int row0,
                                            const float4* __restrict__ qcp, int n) {
   const uint32_t w[4] = {c.x, c.y, c.z, c.w};
@@ -266,6 +277,16 @@ __device__ __forceinline__ float adc16_piv(float s, const uint4 c, const PivTab&
         p = make_float4(xy.x, xy.y, t.z[r], 0.f);
       } else {
         p = t.xyzw[r];
+      }
+      if (IP) {
+        // inner product: e = fma chain of q_i * p_ji from 0; entry = -e, and
+        // s + (-e) is s - e
+        float e = __fmaf_rn(q.x, p.x, 0.f);
+        e = __fmaf_rn(q.y, p.y, e);
+        e = __fmaf_rn(q.z, p.z, e);
+        if (CW > 3) e = __fmaf_rn(q.w, p.w, e);
+        s = __fsub_rn(s, e);
+        continue;
       }
       // the x and y differences in one packed instruction (two independent
       // round-to-nearest subtractions, as __fsub_rn would give)
@@ -425,7 +446,7 @@ __global__ void gather_neighbour_codes(const uint32_t* __restrict__ adj, int adj
 // with at most 32 of them runs one ADC pass instead of NPL. (Without a table,
 // e.g. gann_search_noalloc, every neighbour is evaluated; duplicates of pool
 // entries are then dropped by the rank search.)
-template <typename T, int NPL, int VP, int PIV>
+template <typename T, int NPL, int VP, int PIV, bool IP>
 __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid, uint32_t entry,
                          const WarpSmem& s, const PivTab& piv, int lane, int pl) {
   const int dim = ix.dim, M = ix.chunks, L = a.ef, topk = a.topk;
@@ -442,7 +463,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
   if (vis != nullptr)
     for (int i = 4 * lane; i < (1 << kVisBits); i += 4 * kWarp)
       *reinterpret_cast<uint4*>(vis + i) = make_uint4(kPadId, kPadId, kPadId, kPadId);
-  float qv[VP];   // q'' = (q - c) + c, the lane's dims
+  float qv[VP];   // q'' = (q - c) + c (q for the inner product), the lane's dims
 #pragma unroll
   for (int v = 0; v < VP; ++v) {
     const int i = lane + kWarp * v;
@@ -533,14 +554,14 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
         const float4* qw = s.qcp + 16 * w;
 #pragma unroll
         for (int k = 0; k < NPL; ++k)
-          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, 16)
-                                        : adc16_piv<4>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, 16);
+          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3, IP>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, 16)
+                                        : adc16_piv<4, IP>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, 16);
       } else {
         const float4* qw = s.qcp + 16 * w;
 #pragma unroll
         for (int k = 0; k < NPL; ++k)
-          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, n)
-                                        : adc16_piv<4>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, n);
+          if (ok[k]) dsum[k] = PIV == 3 ? adc16_piv<3, IP>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, n)
+                                        : adc16_piv<4, IP>(dsum[k], cur[k], piv, 16 * w * kPivots, qw, n);
       }
     }
 
@@ -604,14 +625,11 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     float acc = 0.f;
 #pragma unroll
     for (int v = 0; v < VP; ++v) {
-      if (lane + kWarp * v < dim) {
-        const float d = __fsub_rn(qv[v], xv[v]);
-        acc = __fmaf_rn(d, d, acc);
-      }
+      if (lane + kWarp * v < dim) acc = dist_acc<IP>(qv[v], xv[v], acc);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, off));
-    const float ex = __shfl_sync(kFull, acc, 0);
+    const float ex = IP ? -__shfl_sync(kFull, acc, 0) : __shfl_sync(kFull, acc, 0);
     {
       int le = 0;
       for (int t0 = 0; t0 < tcnt; t0 += kWarp) {
@@ -680,7 +698,6 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
           rmin = min(rmin, cr[k]);
         }
       }
-#pragma unroll
       rmin = __reduce_min_sync(kFull, rmin);
       // survivor ranks in key order are non-decreasing: hist[t] = rank of the
       // t-th smallest survivor; entry i >= rmin moves right by #{t : hist[t] <= i}
@@ -765,7 +782,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
 }
 
 // One query per warp, from query setup to the written top-k.
-template <typename T, int NPL, int VP, int PIV>
+template <typename T, int NPL, int VP, int PIV, bool IP>
 __device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchArgs& a, const WarpSmem& s,
                                             const PivTab& piv, int lane, int pl) {
   const int dim = ix.dim;
@@ -784,7 +801,7 @@ __device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchA
     uint32_t entry = static_cast<uint32_t>(ix.medoid);
     if (ix.has_nav) {
       bool capped = false;
-      const int si = nav_search<T>(ix, s.qs, lane, a.nav_max_hops, capped);
+      const int si = nav_search<T, IP>(ix, s.qs, lane, a.nav_max_hops, capped);
       // slot 0 can end up holding an empty slot on degenerate graphs (a node
       // whose only neighbour is itself); the reference then indexes its map out
       // of range, here the query falls back to the medoid and is counted
@@ -793,31 +810,34 @@ __device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchA
       if ((capped || bad) && lane == 0) atomicAdd(a.err + 1, 1);
     }
     __syncwarp();
-    for (int i = lane; i < dim; i += kWarp) s.qs[i] = __fadd_rn(s.qc[i], __ldg(ix.centroid + i));
+    if (!IP)
+      for (int i = lane; i < dim; i += kWarp) s.qs[i] = __fadd_rn(s.qc[i], __ldg(ix.centroid + i));
+    // the table / pivot-mode query terms: q - c for L2, q for the inner product
+    const float* qt = IP ? s.qs : s.qc;
     if (PIV == 0) {
-      build_lut(ix, s.qc, s.lut, lane);
+      build_lut<IP>(ix, qt, s.lut, lane);
     } else {
       for (int c = lane; c < ix.chunks; c += kWarp) {
         const int a0 = __ldg(ix.chunk_off + c), a1 = __ldg(ix.chunk_off + c + 1);
         float r[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) r[i] = a0 + i < a1 ? s.qc[a0 + i] : 0.f;
+        for (int i = 0; i < 4; ++i) r[i] = a0 + i < a1 ? qt[a0 + i] : 0.f;
         s.qcp[c] = make_float4(r[0], r[1], r[2], r[3]);
       }
     }
     __syncwarp();
-    traverse<T, NPL, VP, PIV>(ix, a, qid, entry, s, piv, lane, pl);
+    traverse<T, NPL, VP, PIV, IP>(ix, a, qid, entry, s, piv, lane, pl);
     __syncwarp();
   }
 }
 
 // Table mode: one warp per CTA, the warp's ADC table in its shared memory.
-template <typename T, int NPL, int VP>
+template <typename T, int NPL, int VP, bool IP>
 __global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, const SearchArgs a, int pl) {
   extern __shared__ __align__(16) unsigned char smem[];
   WarpSmem s;
   carve(smem, ix.chunks, ix.dim, NPL, pl, a.topk, &s, false);
-  run_queries<T, NPL, VP, 0>(ix, a, s, PivTab{nullptr, nullptr, nullptr}, threadIdx.x, pl);
+  run_queries<T, NPL, VP, 0, IP>(ix, a, s, PivTab{nullptr, nullptr, nullptr}, threadIdx.x, pl);
 }
 
 // Pivot mode: one persistent CTA per SM holds the 256 x D pivot table once
@@ -827,7 +847,7 @@ __global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, con
 // Queries per SM: 24 at two neighbours per lane (80 registers a thread, no
 // spills); 20 at four, whose extra registers would spill at 24.
 constexpr int piv_warps_max(int npl) { return npl > 2 ? 20 : 24; }
-template <typename T, int NPL, int VP, int CW>
+template <typename T, int NPL, int VP, int CW, bool IP>
 __global__ void __launch_bounds__(kWarp * piv_warps_max(NPL), 1) search_kernel_piv(const DeviceIndex ix, const SearchArgs a,
                                                                           size_t per_warp, int pl) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -852,24 +872,25 @@ __global__ void __launch_bounds__(kWarp * piv_warps_max(NPL), 1) search_kernel_p
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   WarpSmem s;
   carve(smem + piv_tab_bytes(CW, ix.chunks) + per_warp * warp, ix.chunks, ix.dim, NPL, pl, a.topk, &s, true);
-  run_queries<T, NPL, VP, CW>(ix, a, s, piv, lane, pl);
+  run_queries<T, NPL, VP, CW, IP>(ix, a, s, piv, lane, pl);
 }
 
-template <typename T>
+template <bool IP>
 __global__ void __launch_bounds__(kWarp) probe_lut_kernel(const DeviceIndex ix, const float* q, int64_t nq,
                                                           float* lut) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* qc = reinterpret_cast<float*>(smem);
   const int lane = threadIdx.x;
   for (int64_t qid = blockIdx.x; qid < nq; qid += gridDim.x) {
-    for (int i = lane; i < ix.dim; i += kWarp) qc[i] = __fsub_rn(q[qid * ix.dim + i], __ldg(ix.centroid + i));
+    for (int i = lane; i < ix.dim; i += kWarp)
+      qc[i] = IP ? q[qid * ix.dim + i] : __fsub_rn(q[qid * ix.dim + i], __ldg(ix.centroid + i));
     __syncwarp();
-    build_lut(ix, qc, lut + qid * ix.chunks * kPivots, lane);
+    build_lut<IP>(ix, qc, lut + qid * ix.chunks * kPivots, lane);
     __syncwarp();
   }
 }
 
-template <typename T>
+template <typename T, bool IP>
 __global__ void __launch_bounds__(kWarp) probe_entry_kernel(const DeviceIndex ix, const float* q, int64_t nq,
                                                             int32_t* sample, int32_t* entry, int32_t* err,
                                                             int max_hops) {
@@ -880,7 +901,7 @@ __global__ void __launch_bounds__(kWarp) probe_entry_kernel(const DeviceIndex ix
     for (int i = lane; i < ix.dim; i += kWarp) qs[i] = q[qid * ix.dim + i];
     __syncwarp();
     bool capped = false;
-    const int si = nav_search<T>(ix, qs, lane, max_hops, capped);
+    const int si = nav_search<T, IP>(ix, qs, lane, max_hops, capped);
     const bool bad = si < 0 || si >= ix.nav_points;
     if (lane == 0) {
       sample[qid] = si;
@@ -895,7 +916,7 @@ int npl_for(int degree) { return degree <= 64 ? 2 : 4; }
 int pl_for(int ef) { return (ef + kWarp - 1) / kWarp; }
 int vp_for(int dim) { return dim <= 128 ? 4 : 32; }
 
-template <typename T, int NPL, int VP>
+template <typename T, int NPL, int VP, bool IP>
 cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
@@ -911,7 +932,7 @@ cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_co
     if (ix.piv_warps > 0) warps = std::min(warps, ix.piv_warps);
     if (warps >= 8) {
       const size_t smem = tab + per_warp * warps;
-      auto fn = ix.piv_width == 3 ? search_kernel_piv<T, NPL, VP, 3> : search_kernel_piv<T, NPL, VP, 4>;
+      auto fn = ix.piv_width == 3 ? search_kernel_piv<T, NPL, VP, 3, IP> : search_kernel_piv<T, NPL, VP, 4, IP>;
       cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (e != cudaSuccess) return e;
       int64_t grid = std::min<int64_t>(sm_count, (a.nq + warps - 1) / warps);
@@ -921,7 +942,7 @@ cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_co
     }
   }
   const size_t smem = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, false);
-  auto fn = search_kernel<T, NPL, VP>;
+  auto fn = search_kernel<T, NPL, VP, IP>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   int per_sm = 0;
@@ -937,8 +958,10 @@ cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_co
 
 template <typename T, int VP>
 cudaError_t launch_vp(const DeviceIndex& ix, const SearchArgs& a, int sm_count, cudaStream_t st) {
-  if (npl_for(ix.degree) == 2) return launch_variant<T, 2, VP>(ix, a, sm_count, st);
-  return launch_variant<T, 4, VP>(ix, a, sm_count, st);
+  const bool ip = ix.metric == GANN_METRIC_IP;
+  if (npl_for(ix.degree) == 2)
+    return ip ? launch_variant<T, 2, VP, true>(ix, a, sm_count, st) : launch_variant<T, 2, VP, false>(ix, a, sm_count, st);
+  return ip ? launch_variant<T, 4, VP, true>(ix, a, sm_count, st) : launch_variant<T, 4, VP, false>(ix, a, sm_count, st);
 }
 
 template <typename T>
@@ -960,7 +983,7 @@ cudaError_t launch_typed(const DeviceIndex& ix, const SearchArgs& a, int sm_coun
 
 // Query setup: q'' and the ADC table of each query, its entry node, empty
 // pool and top-k.
-template <typename T>
+template <typename T, bool IP>
 __global__ void __launch_bounds__(128) hop_begin_kernel(const DeviceIndex ix, const float* __restrict__ q,
                                                         const HopState s) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -974,18 +997,18 @@ __global__ void __launch_bounds__(128) hop_begin_kernel(const DeviceIndex ix, co
     float* qpp = s.qpp + qid * ix.dim;
     for (int i = lane; i < ix.dim; i += kWarp) {
       const float c = __ldg(ix.centroid + i);
-      const float d = __fsub_rn(qq[i], c);
-      const float r = __fadd_rn(d, c);
+      const float d = IP ? qq[i] : __fsub_rn(qq[i], c);
+      const float r = IP ? qq[i] : __fadd_rn(d, c);
       qc[i] = d;
       qs[i] = r;
       qpp[i] = r;
     }
     __syncwarp();
-    build_lut(ix, qc, s.lut + qid * ix.chunks * kPivots, lane);
+    build_lut<IP>(ix, qc, s.lut + qid * ix.chunks * kPivots, lane);
     uint32_t entry = static_cast<uint32_t>(ix.medoid);
     if (ix.has_nav) {
       bool capped = false;
-      const int si = nav_search<T>(ix, qs, lane, s.nav_max_hops, capped);
+      const int si = nav_search<T, IP>(ix, qs, lane, s.nav_max_hops, capped);
       const bool bad = si < 0 || si >= ix.nav_points;
       if (!bad) entry = static_cast<uint32_t>(__ldg(ix.nav_map + si));
       if ((capped || bad) && lane == 0) atomicAdd(s.err + 1, 1);
@@ -1010,7 +1033,7 @@ __global__ void __launch_bounds__(128) hop_begin_kernel(const DeviceIndex ix, co
 // the next request = the first unvisited pool entry (-1: the query is done).
 // Neighbour ids past the index, or a degree past the slots, count as bad
 // records (err[2]) and are dropped.
-template <typename T>
+template <typename T, bool IP>
 __global__ void __launch_bounds__(128) hop_step_kernel(const DeviceIndex ix, const HopState s,
                                                        const uint8_t* __restrict__ pages, int node_len, int npp) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -1039,7 +1062,7 @@ __global__ void __launch_bounds__(128) hop_step_kernel(const DeviceIndex ix, con
       deg = deg < 0 ? 0 : R;
     }
     // re-rank u on q'' and insert after every equal top-k entry (retset_push_32)
-    const float ex = warp_sqdist<T>(s.qpp + qid * ix.dim, vec, ix.dim, lane);
+    const float ex = warp_dist<T, IP>(s.qpp + qid * ix.dim, vec, ix.dim, lane);
     if (lane == 0) {
       const int cnt = s.found[qid];
       int32_t* nn = s.nns + qid * s.topk;
@@ -1144,8 +1167,14 @@ cudaError_t launch_hop_begin(const DeviceIndex& ix, const float* d_q, const HopS
   const int wpb = 4;
   const size_t smem = sizeof(float) * 2 * ((ix.dim + 3) & ~3) * wpb;
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((s.nq + wpb - 1) / wpb, 148 * 16));
-  if (dtype == 0) hop_begin_kernel<uint8_t><<<grid, kWarp * wpb, smem, st>>>(ix, d_q, s);
-  else hop_begin_kernel<float><<<grid, kWarp * wpb, smem, st>>>(ix, d_q, s);
+  const bool ip = ix.metric == GANN_METRIC_IP;
+  if (dtype == 0) {
+    if (ip) hop_begin_kernel<uint8_t, true><<<grid, kWarp * wpb, smem, st>>>(ix, d_q, s);
+    else hop_begin_kernel<uint8_t, false><<<grid, kWarp * wpb, smem, st>>>(ix, d_q, s);
+  } else {
+    if (ip) hop_begin_kernel<float, true><<<grid, kWarp * wpb, smem, st>>>(ix, d_q, s);
+    else hop_begin_kernel<float, false><<<grid, kWarp * wpb, smem, st>>>(ix, d_q, s);
+  }
   return cudaGetLastError();
 }
 
@@ -1154,16 +1183,15 @@ cudaError_t launch_hop_step(const DeviceIndex& ix, const HopState& s, const uint
   if (s.nq <= 0) return cudaSuccess;
   const int wpb = 4;
   const size_t smem = sizeof(uint64_t) * (2 * static_cast<size_t>(ix.degree) + s.ef) * wpb;
+  const bool ip = ix.metric == GANN_METRIC_IP;
+  auto fn = dtype == 0 ? (ip ? hop_step_kernel<uint8_t, true> : hop_step_kernel<uint8_t, false>)
+                       : (ip ? hop_step_kernel<float, true> : hop_step_kernel<float, false>);
   if (smem > 48 * 1024) {
-    auto f8 = hop_step_kernel<uint8_t>;
-    auto f32 = hop_step_kernel<float>;
-    cudaError_t e = cudaFuncSetAttribute(dtype == 0 ? f8 : f32, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((s.nq + wpb - 1) / wpb, 148 * 16));
-  if (dtype == 0) hop_step_kernel<uint8_t><<<grid, kWarp * wpb, smem, st>>>(ix, s, d_pages, node_len, nodes_per_page);
-  else hop_step_kernel<float><<<grid, kWarp * wpb, smem, st>>>(ix, s, d_pages, node_len, nodes_per_page);
+  fn<<<grid, kWarp * wpb, smem, st>>>(ix, s, d_pages, node_len, nodes_per_page);
   return cudaGetLastError();
 }
 
@@ -1204,7 +1232,8 @@ cudaError_t launch_probe_lut(const DeviceIndex& ix, const float* d_q, int64_t nq
   const size_t smem = sizeof(float) * ((ix.dim + 3) & ~3);
   const unsigned grid = static_cast<unsigned>(nq < 65535 ? nq : 65535);
   if (grid == 0) return cudaSuccess;
-  probe_lut_kernel<float><<<grid, kWarp, smem, st>>>(ix, d_q, nq, d_lut);
+  if (ix.metric == GANN_METRIC_IP) probe_lut_kernel<true><<<grid, kWarp, smem, st>>>(ix, d_q, nq, d_lut);
+  else probe_lut_kernel<false><<<grid, kWarp, smem, st>>>(ix, d_q, nq, d_lut);
   return cudaGetLastError();
 }
 
@@ -1214,10 +1243,10 @@ cudaError_t launch_probe_entry(const DeviceIndex& ix, const float* d_q, int64_t 
   const unsigned grid = static_cast<unsigned>(nq < 65535 ? nq : 65535);
   if (grid == 0) return cudaSuccess;
   const int cap = 1 << 20;
-  if (dtype == GANN_UINT8)
-    probe_entry_kernel<uint8_t><<<grid, kWarp, smem, st>>>(ix, d_q, nq, d_sample, d_entry, d_err, cap);
-  else
-    probe_entry_kernel<float><<<grid, kWarp, smem, st>>>(ix, d_q, nq, d_sample, d_entry, d_err, cap);
+  const bool ip = ix.metric == GANN_METRIC_IP;
+  auto fn = dtype == GANN_UINT8 ? (ip ? probe_entry_kernel<uint8_t, true> : probe_entry_kernel<uint8_t, false>)
+                                : (ip ? probe_entry_kernel<float, true> : probe_entry_kernel<float, false>);
+  fn<<<grid, kWarp, smem, st>>>(ix, d_q, nq, d_sample, d_entry, d_err, cap);
   return cudaGetLastError();
 }
 

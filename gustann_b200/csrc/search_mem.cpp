@@ -4,6 +4,9 @@
 //
 //   search_mem --query Q --index I --pq_data P [--nav_graph N] --data_type uint8|float
 //              [--ground_truth GT] [--topk K] --ef_search L [L2 ...] [-R repeat] [-G]
+//              [--output FILE]
+// --output writes the ids of the (last) ef_search as a `bin` file of int32
+// (npts, k, ids), the result file check_recall reads.
 #include <sys/stat.h>
 
 #include <cstdio>
@@ -66,6 +69,7 @@ void usage() {
                "                  [--nav_graph DIR] [--ground_truth FILE] [--topk K]\n"
                "                  --ef_search L [L ...] [-R|--repeat N] [-G|--use-gpu-mem] [--device D]\n"
                "                  [--hybrid -B|--minibatch N -T|--thread N [--io_backend memory]]\n"
+               "                  [--output FILE]  ids of the last ef_search as a bin file (check_recall)\n"
                "  --hybrid: records stay in the index file and each hop reads the needed pages\n"
                "            (the reference driver's HYBRID_CALC build, GustANN::init_hybrid)\n");
   std::exit(1);
@@ -74,7 +78,7 @@ void usage() {
 }  // namespace
 
 int main(int argc, char** argv) {
-  std::string query_file, gt_file, data_type;
+  std::string query_file, gt_file, data_type, out_file;
   gustann::GustANNConfig cfg;
   int topk = 100, repeat = 20, device = 0;
   bool use_gpu_mem = false, hybrid = false;
@@ -96,6 +100,7 @@ int main(int argc, char** argv) {
     else if (a == "--repeat" || a == "-R") repeat = std::atoi(need().c_str());
     else if (a == "--use-gpu-mem" || a == "-G") use_gpu_mem = true;
     else if (a == "--device") device = std::atoi(need().c_str());
+    else if (a == "--output") out_file = need();
     else if (a == "--hybrid") hybrid = true;
     else if (a == "--minibatch" || a == "-B") hcfg.mini_batch = std::atoi(need().c_str());
     else if (a == "--thread" || a == "-T") hcfg.thread_cnt = std::atoi(need().c_str());
@@ -196,6 +201,17 @@ int main(int argc, char** argv) {
   } catch (const std::exception& e) {
     std::fprintf(stderr, "%s\n", e.what());
     return 1;
+  }
+  if (!out_file.empty()) {
+    FILE* f = std::fopen(out_file.c_str(), "wb");
+    const int32_t head[2] = {static_cast<int32_t>(nq), topk};
+    const bool ok = f && std::fwrite(head, 4, 2, f) == 2 &&
+                    std::fwrite(nns.get(), 4, nq * topk, f) == nq * static_cast<size_t>(topk);
+    if (f) std::fclose(f);
+    if (!ok) {
+      std::fprintf(stderr, "cannot write %s\n", out_file.c_str());
+      return 1;
+    }
   }
   return 0;
 }

@@ -110,40 +110,53 @@ def record_geometry(num_dims: int, elem: int, max_m0: int) -> tuple[int, int]:
     return node_len, PAGE_SIZE // node_len
 
 
-def write_disk_index(path: str, vectors: np.ndarray, adj: np.ndarray, deg: np.ndarray,
-                     medoid: int, max_m0: int | None = None) -> DiskLayout:
+def _rows(x, a: int, b: int) -> np.ndarray:
+    """Rows [a, b) of a numpy array or a (possibly CUDA) torch tensor, as numpy."""
+    if hasattr(x, "detach"):
+        return x[a:b].detach().cpu().numpy()
+    return np.asarray(x[a:b])
+
+
+def write_disk_index(path: str, vectors, adj, deg, medoid: int, max_m0: int | None = None,
+                     chunk_pages: int = 1 << 16) -> DiskLayout:
     """Write records ``[T x D vector][u32 deg][u32 nbr x max_m0]`` into 4 KB pages.
 
     ``adj`` is ``[N, >=max(deg)]`` int; entries past ``deg`` are ignored (zero-filled
     on disk). The header is DiskANN's metadata ``bin<u64>`` (9 values).
+    ``vectors``, ``adj`` and ``deg`` may be numpy arrays or torch tensors (also on
+    a GPU); the file is written ``chunk_pages`` pages at a time, so host memory
+    stays bounded at any N.
     """
     n, d = vectors.shape
-    elem = vectors.dtype.itemsize
+    elem = np.dtype(str(vectors.dtype).replace("torch.", "")).itemsize
     if max_m0 is None:
         max_m0 = int(adj.shape[1])
     node_len, npp = record_geometry(d, elem, max_m0)
     num_pages = (n + npp - 1) // npp
     file_size = (num_pages + 1) * PAGE_SIZE
 
-    rec = np.zeros((num_pages * npp, node_len), dtype=np.uint8)
-    rec[:n, : d * elem] = np.ascontiguousarray(vectors).view(np.uint8).reshape(n, d * elem)
-    deg = np.asarray(deg, dtype=np.uint32)
-    nb = np.zeros((n, max_m0), dtype=np.uint32)
-    w = min(max_m0, adj.shape[1])
-    mask = np.arange(w)[None, :] < deg[:, None]
-    nb[:, :w] = np.where(mask, adj[:, :w], 0).astype(np.uint32)
-    rec[:n, d * elem: d * elem + 4] = deg.reshape(n, 1).view(np.uint8)
-    rec[:n, d * elem + 4:] = nb.view(np.uint8)
-    pages = np.zeros((num_pages, PAGE_SIZE), dtype=np.uint8)
-    pages[:, : npp * node_len] = rec.reshape(num_pages, npp * node_len)
-
     meta = np.array([n, d, medoid, node_len, npp, 0, 0, 0, file_size], dtype=np.uint64)
     header = np.zeros(PAGE_SIZE, dtype=np.uint8)
     hb = struct.pack("<II", len(meta), 1) + meta.tobytes()
     header[: len(hb)] = np.frombuffer(hb, dtype=np.uint8)
+    w = min(max_m0, adj.shape[1])
     with open(path, "wb") as f:
         f.write(header.tobytes())
-        f.write(pages.tobytes())
+        for p0 in range(0, num_pages, chunk_pages):
+            p1 = min(num_pages, p0 + chunk_pages)
+            r0, r1 = p0 * npp, min(n, p1 * npp)
+            m = r1 - r0
+            rec = np.zeros(((p1 - p0) * npp, node_len), dtype=np.uint8)
+            rec[:m, : d * elem] = np.ascontiguousarray(_rows(vectors, r0, r1)).view(np.uint8).reshape(m, d * elem)
+            dg = _rows(deg, r0, r1).astype(np.uint32)
+            a = _rows(adj, r0, r1)[:, :w]
+            nb = np.zeros((m, max_m0), dtype=np.uint32)
+            nb[:, :w] = np.where(np.arange(w)[None, :] < dg[:, None], a, 0).astype(np.uint32)
+            rec[:m, d * elem: d * elem + 4] = dg.reshape(m, 1).view(np.uint8)
+            rec[:m, d * elem + 4:] = nb.view(np.uint8)
+            pages = np.zeros((p1 - p0, PAGE_SIZE), dtype=np.uint8)
+            pages[:, : npp * node_len] = rec.reshape(p1 - p0, npp * node_len)
+            f.write(pages.tobytes())
     return DiskLayout(n, d, medoid, node_len, npp, d * elem, max_m0, num_pages)
 
 
@@ -243,14 +256,23 @@ def write_nav(directory: str, sample_vectors: np.ndarray, sample_ids: np.ndarray
         if max_degree < max_deg:
             raise ValueError("max_degree below the largest node degree")
         max_deg = max_degree
-    body = bytearray()
-    for i in range(s):
-        k = int(deg[i])
-        body += struct.pack("<I", k) + np.asarray(adj[i, :k], dtype=np.uint32).tobytes()
-    size = 24 + len(body)
+    # per node: u32 degree, then its first `degree` neighbour ids
+    adj = np.asarray(adj)
+    w = adj.shape[1] if adj.ndim == 2 else 0
+    if s and int(deg.max()) > w:
+        raise ValueError("a degree exceeds the adjacency width")
+    keep = np.arange(w)[None, :] < deg[:, None] if s else np.zeros((0, 0), bool)
+    body = np.zeros(s + int(deg.sum()), dtype=np.uint32)
+    starts = np.arange(s, dtype=np.int64) + np.concatenate([[0], np.cumsum(deg, dtype=np.int64)[:-1]]) if s else \
+        np.zeros(0, np.int64)
+    body[starts] = deg
+    if s:
+        slot = starts[:, None] + 1 + np.arange(w)[None, :]
+        body[slot[keep]] = adj[keep].astype(np.uint32)
+    size = 24 + 4 * body.size
     with open(os.path.join(directory, "nav_index"), "wb") as f:
         f.write(struct.pack("<QIIQ", size, max_deg, int(start), 0))
-        f.write(bytes(body))
+        f.write(body.tobytes())
     write_bin(os.path.join(directory, "nav_index.data"), np.ascontiguousarray(sample_vectors))
     with open(os.path.join(directory, "map.txt"), "w") as f:
         f.write("".join(f"{int(x)}\n" for x in sample_ids))

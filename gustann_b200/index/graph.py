@@ -213,26 +213,33 @@ def long_range_candidates(X: torch.Tensor, gen: torch.Generator, per_level: int,
     return torch.cat(ids_l, 1), torch.cat(d_l, 1)
 
 
-def reachable(adj: torch.Tensor, entry: int) -> torch.Tensor:
-    """Boolean mask of nodes reachable from ``entry`` along out-edges."""
+def reachable(adj: torch.Tensor, entry: int, block: int = 1 << 22) -> torch.Tensor:
+    """Boolean mask of nodes reachable from ``entry`` along out-edges
+    (breadth-first; each level marks its neighbours with a scatter, so no sort
+    of the frontier is needed at any size)."""
     n = adj.shape[0]
     seen = torch.zeros(n, dtype=torch.bool, device=adj.device)
+    mark = torch.zeros(n, dtype=torch.bool, device=adj.device)
     frontier = torch.tensor([entry], device=adj.device, dtype=torch.int64)
     seen[frontier] = True
     while frontier.numel():
-        nb = adj[frontier].reshape(-1).to(torch.int64)
-        nb = nb[nb >= 0]
-        nb = nb[~seen[nb]].unique()
-        seen[nb] = True
-        frontier = nb
+        mark.zero_()
+        for s in range(0, frontier.numel(), block):
+            nb = adj[frontier[s: s + block]].reshape(-1).to(torch.int64)
+            mark[nb[nb >= 0]] = True
+        mark &= ~seen
+        seen |= mark
+        frontier = torch.nonzero(mark).reshape(-1)
     return seen
 
 
-def repair_connectivity(X: torch.Tensor, adj: torch.Tensor, entry: int, rounds: int = 64) -> torch.Tensor:
+def repair_connectivity(X: torch.Tensor, adj: torch.Tensor, entry: int, rounds: int = 64,
+                        inplace: bool = False) -> torch.Tensor:
     """Give every node a path from ``entry``: an unreachable node gets an edge
     from its nearest reachable node, written into that node's free slot or, if
-    it has none, over its last (farthest) edge. Repeats until all are reached."""
-    adj = adj.clone()
+    it has none, over its last (farthest) edge. Repeats until all are reached.
+    ``adj`` keeps its dtype; ``inplace`` edits it instead of a copy."""
+    adj = adj if inplace else adj.clone()
     n, R = adj.shape
     for _ in range(rounds):
         seen = reachable(adj, entry)
@@ -240,7 +247,13 @@ def repair_connectivity(X: torch.Tensor, adj: torch.Tensor, entry: int, rounds: 
             break
         un = torch.nonzero(~seen).reshape(-1)
         rs = torch.nonzero(seen).reshape(-1)
-        near, _ = knn_exact(X[rs], X[un], 1)
+        Xr, Xu = X[rs], X[un]
+        if X.is_cuda and X.dtype in (torch.uint8, torch.float32) and (X.shape[1] * X.element_size()) % 16 == 0:
+            from ..api import exact_knn
+            near = exact_knn(Xr, Xu, 1)[0].long()
+        else:
+            near, _ = knn_exact(Xr, Xu, 1)
+        del Xr, Xu
         src = rs[near[:, 0]]
         # one new edge per source node per round keeps the replacement local
         order = torch.argsort(src, stable=True)

@@ -69,7 +69,7 @@ def build_index(root: str, X: torch.Tensor, dtype: int, R: int = 64, alpha: floa
             from .vamana import vamana_graph
             a, d, m = vamana_graph(Xg, codes_g, pivots, centroid, offs, R=R_g, L=L_g, alpha=alpha,
                                    passes=passes, seed=seed_g, verbose=verbose)
-            a = repair_connectivity(Xg, a.long(), m).to(torch.int32)
+            a = repair_connectivity(Xg, a, m, inplace=True)
             return a, (a >= 0).sum(1).to(torch.int32), m
         a, d = build_graph(Xg, R_g, alpha=alpha, seed=seed_g, long_range=long_range)
         return a, d, medoid(Xg)
@@ -82,9 +82,7 @@ def build_index(root: str, X: torch.Tensor, dtype: int, R: int = 64, alpha: floa
               flush=True)
 
     t0 = time.time()
-    Xn = _to_numpy(X, dtype)
-    formats.write_disk_index(paths["index_file"], Xn, adj.cpu().numpy(), deg.cpu().numpy(), med, max_m0=R)
-    del Xn
+    formats.write_disk_index(paths["index_file"], X, adj, deg, med, max_m0=R)
     t["write_s"] = time.time() - t0
 
     if nav:

@@ -11,7 +11,9 @@ Each batch's greedy searches are one launch of the fused CUDA search kernel
 over the graph being built (``gann_open_device`` on tensors this module
 mutates between batches): entry = medoid, ``ef = topk = L``, so the kernel
 returns the ``L`` nearest expanded nodes with exact distances -- the candidate
-set. Pruning and reverse-edge merging are batched torch ops on the same GPU.
+set. RobustPrune runs as one CUDA launch per step (``gann_robust_prune``, a
+CTA per point); candidate merging and reverse edges are batched torch ops on
+the same GPU.
 """
 from __future__ import annotations
 
@@ -20,7 +22,7 @@ import time
 import numpy as np
 import torch
 
-from .graph import _dedup_sorted_rows, _f32, medoid, robust_prune
+from .graph import _f32, medoid
 
 
 def _pad_rows(t: torch.Tensor, mult_bytes: int = 16) -> torch.Tensor:
@@ -36,14 +38,16 @@ def _pad_rows(t: torch.Tensor, mult_bytes: int = 16) -> torch.Tensor:
 def vamana_graph(X: torch.Tensor, codes: np.ndarray, pivots: np.ndarray, centroid: np.ndarray,
                  offs: np.ndarray, R: int = 64, L: int = 100, alpha: float = 1.2, passes: int = 2,
                  seed: int = 0, max_frac: float = 0.02, verbose: bool = False, med: int | None = None):
-    """Return (adj [n,R] int32 -1-padded, deg [n] int32, medoid) for CUDA tensor ``X``."""
+    """Return (adj [n,R] int32 -1-padded, deg [n] int32, medoid) for CUDA tensor ``X``.
+
+    uint8 vectors are widened to float32 only in the rows a step touches, so
+    the builder holds no float copy of the base set."""
     from ..api import GustANN
 
     assert X.is_cuda, "the Vamana builder runs on the GPU"
     dev = X.device
     n = X.shape[0]
     L = max(L, 8)
-    Xf = _f32(X).contiguous()
     vec = _pad_rows(X.contiguous())
     cd_dev = torch.from_numpy(np.ascontiguousarray(codes)).to(dev)
     cd_dev = _pad_rows(cd_dev)
@@ -57,27 +61,38 @@ def vamana_graph(X: torch.Tensor, codes: np.ndarray, pivots: np.ndarray, centroi
     alphas = [1.0, alpha] if passes >= 2 else [alpha]
     stream = torch.cuda.current_stream(dev)
     maxb = max(1, int(max_frac * n))
-    prune_batch = 1 << 15
+
+    def prune(rows, ci, cd, a):
+        from ..api import robust_prune as gpu_prune
+        return gpu_prune(vec, rows, ci[:, :256], cd[:, :256], R, a)
+
+    def merge(ids2, d2):
+        from ..api import sort_unique_rows
+        return sort_unique_rows(ids2, d2)
+
+    chunk = 1 << 20      # reverse-edge targets merged per step (bounds the temporaries)
+    ar = torch.arange(max(L, R), device=dev)
 
     def insert(ids: torch.Tensor, a: float):
         b = ids.shape[0]
-        q = Xf[ids].contiguous()
+        q = _f32(X[ids]).contiguous()
         nns = torch.empty((b, L), dtype=torch.int32, device=dev)
         dst = torch.empty((b, L), dtype=torch.float32, device=dev)
         fnd = torch.empty(b, dtype=torch.int32, device=dev)
         g.search_device(q.data_ptr(), b, L, L, nns.data_ptr(), dst.data_ptr(), fnd.data_ptr(), 0,
                         stream.cuda_stream)
-        valid = torch.arange(L, device=dev)[None, :] < fnd[:, None]
-        ci = torch.where(valid, nns.long(), torch.full_like(nns, -1, dtype=torch.int64))
+        valid = ar[None, :L] < fnd[:, None]
+        ci = torch.where(valid, nns, torch.full_like(nns, -1))
         cdv = torch.where(valid, dst, torch.full_like(dst, float("inf")))
-        ci, cdv = _dedup_sorted_rows(torch.cat([ci, adj[ids, :R].long()], 1), torch.cat([cdv, adjd[ids]], 1))
-        new, newd = robust_prune(Xf, ids, ci, cdv, R, a, batch=prune_batch, return_dist=True)
-        adj[ids, :R] = new.to(torch.int32)
+        ci, cdv = merge(torch.cat([ci, adj[ids, :R]], 1), torch.cat([cdv, adjd[ids]], 1))
+        new, newd = prune(ids, ci, cdv, a)
+        adj[ids, :R] = new
         adjd[ids] = newd
-        # reverse edges, closest R offers per target
+        # reverse edges: target t is offered p for each kept edge p -> t, its R
+        # closest offers are merged with its row, and an overfull row is pruned
         m = new >= 0
-        src = ids[:, None].expand_as(new)[m]
-        tgt = new[m]
+        src = ids[:, None].expand_as(new)[m].to(torch.int32)
+        tgt = new[m].long()
         td = newd[m]
         o = torch.argsort(td, stable=True)
         src, tgt, td = src[o], tgt[o], td[o]
@@ -85,26 +100,25 @@ def vamana_graph(X: torch.Tensor, codes: np.ndarray, pivots: np.ndarray, centroi
         src, tgt, td = src[o], tgt[o], td[o]
         uq, cnt = torch.unique_consecutive(tgt, return_counts=True)
         first = torch.cumsum(cnt, 0) - cnt
-        grp = torch.repeat_interleave(torch.arange(uq.shape[0], device=dev), cnt)
-        rank = torch.arange(tgt.shape[0], device=dev) - first[grp]
-        keep = rank < R
-        inc = torch.full((uq.shape[0], R), -1, dtype=torch.int64, device=dev)
-        incd = torch.full((uq.shape[0], R), float("inf"), device=dev)
-        inc[grp[keep], rank[keep]] = src[keep]
-        incd[grp[keep], rank[keep]] = td[keep]
-        ui, ud = _dedup_sorted_rows(torch.cat([adj[uq, :R].long(), inc], 1), torch.cat([adjd[uq], incd], 1))
-        tot = (ui >= 0).sum(1)
-        fit = tot <= R
-        if bool(fit.any()):
-            f = uq[fit]
-            adj[f, :R] = ui[fit, :R].to(torch.int32)
+        take = cnt.clamp_max(R)
+        last = max(tgt.shape[0] - 1, 0)
+        for c0 in range(0, uq.shape[0], chunk):
+            u = uq[c0: c0 + chunk]
+            pos = (first[c0: c0 + chunk, None] + ar[None, :R]).clamp_max(last)
+            ok = ar[None, :R] < take[c0: c0 + chunk, None]
+            inc = torch.where(ok, src[pos], torch.full_like(pos, -1, dtype=torch.int32))
+            incd = torch.where(ok, td[pos], torch.full_like(pos, float("inf"), dtype=torch.float32))
+            ui, ud = merge(torch.cat([adj[u, :R], inc], 1), torch.cat([adjd[u], incd], 1))
+            fit = ui[:, R] < 0
+            f = u[fit]
+            adj[f, :R] = ui[fit, :R]
             adjd[f] = ud[fit, :R]
-        over = ~fit
-        if bool(over.any()):
-            rows = uq[over]
-            pi, pd = robust_prune(Xf, rows, ui[over], ud[over], R, a, batch=prune_batch, return_dist=True)
-            adj[rows, :R] = pi.to(torch.int32)
-            adjd[rows] = pd
+            over = ~fit
+            rows = u[over]
+            if rows.numel():
+                pi, pd = prune(rows, ui[over], ud[over], a)
+                adj[rows, :R] = pi
+                adjd[rows] = pd
 
     t0 = time.time()
     old_tf32 = torch.backends.cuda.matmul.allow_tf32

@@ -40,6 +40,10 @@ typedef enum {
 /* Element type of the stored vectors: gustann::DataType (src/common.hpp:22-25). */
 typedef enum { GANN_UINT8 = 0, GANN_FLOAT = 1 } gann_dtype;
 
+/* Distance: squared L2 (the reference's only metric, src/common.hpp:28-30) or
+ * inner product, searched as the distance -<q, x> so that smaller is nearer. */
+typedef enum { GANN_METRIC_L2 = 0, GANN_METRIC_IP = 1 } gann_metric;
+
 /*
  * Index location and placement. Replaces gustann::GustANNConfig
  * (src/ssd_search.hpp:18-23) plus the use_gpu_mem flag of
@@ -73,6 +77,11 @@ typedef enum { GANN_UINT8 = 0, GANN_FLOAT = 1 } gann_dtype;
  *                     first search. -1 loads every range into its own
  *                     allocation on this device (single-device use of the
  *                     split addressing, e.g. for tests).
+ *   metric            GANN_METRIC_L2 (0, the reference's) or GANN_METRIC_IP:
+ *                     ADC entries, pivot-graph and exact distances all become
+ *                     -<q, x> (table entry -(sum of q_i * p_ji) per chunk);
+ *                     the index files are the same. No counterpart in the
+ *                     reference, which is L2-only (src/common.hpp:28-30).
  */
 typedef struct {
   const char* index_file;
@@ -84,7 +93,8 @@ typedef struct {
   int32_t layout;
   int32_t part_count;
   int32_t part_index;
-  int32_t reserved[2];
+  int32_t metric;
+  int32_t reserved[1];
 } gann_config;
 
 /* Replaces gustann::GustANNStats (src/ssd_search.hpp:25-27) and adds the
@@ -173,7 +183,8 @@ typedef struct {
   int32_t dtype;
   int64_t medoid;
   int32_t device;
-  int32_t reserved[3];
+  int32_t metric;          /* GANN_METRIC_L2 or GANN_METRIC_IP, as gann_config */
+  int32_t reserved[2];
 } gann_device_index;
 
 int gann_open_device(const gann_device_index* desc, gann_handle** out);
@@ -191,11 +202,19 @@ int gann_open_device(const gann_device_index* desc, gann_handle** out);
  * loading the library holds until exit. The table space needed is about
  * 2048*dim + 4096*pq_chunks bytes; an index needing more than the array is
  * rejected with GANN_EUNSUPPORTED. The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress); make that first call before
- * any stream capture. All calls share the one array and each call re-stages
- * it, so calls whose work overlaps on the GPU race: serialise them (one stream,
- * or wait for the previous call). Asynchronous on `stream`; results are the
- * same as gann_search_device over the same arrays.
+ * array's device address (cudaGetSymbolAddress) and keeps it for the life of
+ * the process; make that first call before any stream capture. The address
+ * belongs to the device's primary context: call from that context, and a
+ * cudaDeviceReset ends the array's use by this entry point for the process.
+ * All calls share the one array and each call re-stages it, so calls whose
+ * work overlaps on the GPU race: serialise them (one stream, or wait for the
+ * previous call). Asynchronous on `stream`: desc's host arrays (pivots,
+ * centroid, chunk offsets) are read by copies enqueued on the stream; ordinary
+ * pageable arrays may be reused when the call returns, page-locked ones must
+ * stay unchanged until the stream has passed the call. Results are the same as
+ * gann_search_device over the same arrays. Queries stopped by the hop cap are
+ * not reported by this entry point (it has no statistics output). The
+ * caller's current device is left as it was.
  * No counterpart in the reference, which allocates per search call
  * (src/pure_mem.cu:78-89).
  */
@@ -289,6 +308,46 @@ int gann_probe_entry(gann_handle* h, const float* queries, int64_t nq,
  * driven by std::mt19937(seed) -- the sampling step of bin/gen_small_file.cpp:18-40
  * (seed 114514 there). Host only. */
 int gann_pivot_sample(int64_t n, int64_t s, uint32_t seed, int32_t* out);
+
+/* Exact k nearest neighbours by brute force on the GPU: the ground truth that
+ * recall@k is computed against (the reference reads it from an ivecs file,
+ * bin/search_disk.cpp:206-213, and computes recall with calc_recall,
+ * bin/utils.hpp:104-116; the file itself comes from tools outside the
+ * reference). Device buffers on `device`, enqueued on `stream`:
+ *   base      [num_points rows x base_stride bytes], `dim` elements of dtype
+ *   queries   [nq rows x query_stride bytes], same dtype as the base (uint8
+ *             queries as uint8); strides and both pointers 16-byte aligned
+ *   ids       [nq x k] int32, distances [nq x k] float32, ascending by
+ *             (distance, id); L2 distances are squared (exact integers for
+ *             uint8 data), IP distances are -<q, x>.
+ * 1 <= k <= 128. Allocates temporary device memory on the stream
+ * (cudaMallocAsync). */
+int gann_exact_knn(const void* d_base, int64_t num_points, int64_t base_stride, int32_t dim, int32_t dtype,
+                   const void* d_queries, int64_t query_stride, int64_t nq, int32_t k, int32_t metric,
+                   int32_t* d_ids, float* d_distances, int32_t device, void* stream);
+
+/* RobustPrune (Subramanya et al., NeurIPS 2019) of `count` points at once, for
+ * building the graph the search runs on (the reference takes its indexes from
+ * DiskANN's builder, an empty submodule in its tree). Point i = points[i] has
+ * `k` candidates cand[i * k ..] sorted nearest-first (-1 = empty), with their
+ * squared L2 distances cand_dist[i * k ..] to the point; the nearest live
+ * candidate c is kept and every later live candidate c' with
+ * alpha * |c - c'|^2 <= cand_dist(c') is dropped, until r are kept. Writes
+ * out [count x r] int32 (nearest-first, -1 padded) and out_dist [count x r]
+ * (+inf padded). Device buffers on `device`, enqueued on `stream`; vectors
+ * [num_points rows x stride bytes] of dtype, 16-byte aligned. k <= 256. */
+int gann_robust_prune(const void* d_vectors, int64_t num_points, int64_t stride, int32_t dim, int32_t dtype,
+                      const int32_t* d_points, int64_t count, const int32_t* d_cand, const float* d_cand_dist,
+                      int32_t k, int32_t r, float alpha, int32_t* d_out, float* d_out_dist, int32_t device,
+                      void* stream);
+
+/* Candidate rows for gann_robust_prune: each of `rows` rows of `k` (id,
+ * distance) pairs is sorted by (distance, id) with empty slots (id < 0) and
+ * repeated ids removed (the nearest copy stays), padded with (-1, +inf).
+ * Device buffers, k <= 256; out may not alias in. No counterpart in the
+ * reference (index construction is DiskANN's there). */
+int gann_sort_unique_rows(const int32_t* d_ids, const float* d_dists, int64_t rows, int32_t k, int32_t* d_out_ids,
+                          float* d_out_dists, int32_t device, void* stream);
 
 #ifdef __cplusplus
 }

@@ -17,6 +17,9 @@ namespace gustann {
 // src/common.hpp:22-25
 enum DataType { UINT8 = 0, FLOAT = 1 };
 
+// Distance (an extension: the reference is L2-only, src/common.hpp:28-30).
+enum Metric { L2 = GANN_METRIC_L2, INNER_PRODUCT = GANN_METRIC_IP };
+
 // src/ssd_search.hpp:18-23
 class GustANNConfig {
  public:
@@ -48,7 +51,8 @@ struct HybridExecutorConfig {
 
 class GustANN {
  public:
-  explicit GustANN(DataType data_type = FLOAT, int device = 0) : data_type_(data_type), device_(device) {}
+  explicit GustANN(DataType data_type = FLOAT, int device = 0, Metric metric = L2)
+      : data_type_(data_type), device_(device), metric_(metric) {}
   GustANN(const GustANN&) = delete;
   GustANN& operator=(const GustANN&) = delete;
   ~GustANN() { gann_close(h_); }
@@ -64,6 +68,7 @@ class GustANN {
     c.dtype = data_type_;
     c.use_gpu_mem = use_gpu_mem ? 1 : 0;
     c.device = device_;
+    c.metric = metric_;
     check(gann_open(&c, &h_));
     is_hybrid_ = false;
   }
@@ -82,6 +87,7 @@ class GustANN {
     c.dtype = data_type_;
     c.use_gpu_mem = 2;
     c.device = device_;
+    c.metric = metric_;
     check(gann_open(&c, &h_));
     hybrid_ = hc;
     is_hybrid_ = true;
@@ -155,6 +161,7 @@ class GustANN {
   }
   DataType data_type_;
   int device_;
+  Metric metric_ = L2;
   gann_handle* h_ = nullptr;
   bool is_hybrid_ = false;
   HybridExecutorConfig hybrid_;

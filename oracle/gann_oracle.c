@@ -17,6 +17,11 @@
  * Loaders follow src/layout.cpp:11-69, src/pq_search.cu:56-121,187-201 and
  * src/nav_graph.cu:41-100.
  *
+ * oracle_set_metric(o, 1) switches every distance to the inner product,
+ * searched as -<q, x> (the reference is L2-only, src/common.hpp:28-30; this
+ * is the definition the CUDA path follows): ADC entries -(sum of q_i * p_ji)
+ * per chunk, exact distances -(lane-strided q.x sums, shfl tree), q'' = q.
+ *
  * `fma_mode` selects how the reference's `acc += d * d` statements are
  * evaluated: 1 = fused multiply-add (nvcc's default contraction), 0 = separate
  * multiply and add. Compile with -ffp-contract=off so the C compiler adds no
@@ -44,6 +49,7 @@
 
 typedef struct {
   int dtype, elem, fma_mode;
+  int metric; /* 0: squared L2 (the reference's), 1: inner product as -<q, x> */
   /* disk index */
   int64_t n, dim, medoid, node_len, npp, max_m0, data_size, num_pages;
   uint8_t* pages; /* num_pages * 4096, header page dropped */
@@ -70,6 +76,15 @@ static float sqacc(float acc, float d, int fma_mode) {
   }
 }
 
+/* acc + a * b, fused or not like sqacc */
+static float dotacc(float acc, float a, float b, int fma_mode) {
+  if (fma_mode) return fmaf(a, b, acc);
+  {
+    volatile float p = a * b;
+    return acc + p;
+  }
+}
+
 static float elem_at(const oracle_t* o, const uint8_t* base, int64_t i) {
   if (o->dtype == 0) return (float)base[i];
   {
@@ -88,14 +103,19 @@ static float warp_sq(const oracle_t* o, const float* a, const uint8_t* b) {
     float v = 0.f;
     int64_t i;
     for (i = l; i < o->dim; i += 32) {
-      float d = a[i] - elem_at(o, b, i);
-      v = sqacc(v, d, o->fma_mode);
+      if (o->metric) {
+        v = dotacc(v, a[i], elem_at(o, b, i), o->fma_mode);
+      } else {
+        float d = a[i] - elem_at(o, b, i);
+        v = sqacc(v, d, o->fma_mode);
+      }
     }
     p[l] = v;
   }
   for (off = 16; off > 0; off >>= 1)
     for (l = 0; l < off; ++l) p[l] = p[l] + p[l + off];
-  return p[0];
+  /* inner product: the same lane sums and tree on q.x, negated */
+  return o->metric ? -p[0] : p[0];
 }
 
 /* ------------------------------------------------------------- loading */
@@ -238,6 +258,22 @@ static void lut_one(const oracle_t* o, const float* q, float* lut, float* qc, fl
   int64_t i;
   int j;
   memset(lut, 0, sizeof(float) * o->m * NPIV);
+  if (o->metric) {
+    /* inner product (no counterpart in the reference): entry (c, j) =
+     * -(sum over the chunk's dims, ascending, of q_i * pivot_ji), accumulated
+     * from 0 like the L2 entries; the query is used as given (q'' = q) */
+    for (i = 0; i < o->dim; ++i) {
+      int idx = o->chunk_id[i];
+      for (j = 0; j < NPIV; ++j)
+        lut[idx * NPIV + j] = dotacc(lut[idx * NPIV + j], q[i], o->pivots_t[(size_t)i * NPIV + j], o->fma_mode);
+    }
+    for (j = 0; j < o->m * NPIV; ++j) lut[j] = -lut[j];
+    for (i = 0; i < o->dim; ++i) {
+      qc[i] = q[i];
+      qpp[i] = q[i];
+    }
+    return;
+  }
   for (i = 0; i < o->dim; ++i) qc[i] = q[i] - o->centroid[i];
   for (i = 0; i < o->dim; ++i) {
     int idx = o->chunk_id[i];
@@ -563,4 +599,5 @@ int oracle_search(const oracle_t* o, const float* q, int64_t nq, int topk, int L
 }
 
 int64_t oracle_dim(const oracle_t* o) { return o->dim; }
+void oracle_set_metric(oracle_t* o, int metric) { o->metric = metric ? 1 : 0; }
 int oracle_chunks(const oracle_t* o) { return o->m; }

@@ -19,7 +19,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libgustann_ref.so")
-REF_SRC = os.environ.get("GANN_REFERENCE", "/root/reference")
+# the reference's source tree (GANN_REFERENCE); only needed to build REF_SO
+REF_SRC = os.environ.get("GANN_REFERENCE", "")
 
 F_HOPCAP, F_STALE, F_DUPNBR, F_NAVRACE = 1, 2, 4, 8
 
@@ -27,7 +28,7 @@ F_HOPCAP, F_STALE, F_DUPNBR, F_NAVRACE = 1, 2, 4, 8
 def build(ref: bool = True) -> None:
     """Build the C oracle, and the reference library when its sources exist."""
     targets = ["oracle"]
-    if ref and os.path.isdir(os.path.join(REF_SRC, "src")):
+    if ref and REF_SRC and os.path.isdir(os.path.join(REF_SRC, "src")):
         targets.append("ref")
     subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_SRC}", *targets], check=True)
 
@@ -59,14 +60,17 @@ class Oracle:
             L.oracle_dim.argtypes = [vp]
             L.oracle_chunks.restype = C.c_int
             L.oracle_chunks.argtypes = [vp]
+            L.oracle_set_metric.argtypes = [vp, C.c_int]
             cls._lib = L
         return cls._lib
 
-    def __init__(self, index_file: str, pq_prefix: str, nav_dir: str | None, dtype: int, fma_mode: int = 1):
+    def __init__(self, index_file: str, pq_prefix: str, nav_dir: str | None, dtype: int, fma_mode: int = 1,
+                 metric: int = 0):
         L = self.lib()
         self.h = L.oracle_open(index_file.encode(), pq_prefix.encode(), (nav_dir or "").encode(), dtype, fma_mode)
         if not self.h:
             raise RuntimeError(f"oracle_open failed for {index_file}")
+        L.oracle_set_metric(self.h, metric)
         self.dim = int(L.oracle_dim(self.h))
         self.m = int(L.oracle_chunks(self.h))
 

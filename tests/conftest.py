@@ -47,6 +47,18 @@ INDEXES = {
 }
 
 
+# inner-product indexes (searched with GANN_METRIC_IP; the graph is built on
+# L2 over unit vectors, where both orders agree): configuration 4's text-like
+# mixture with Zipf(1.1) queries, at 96 dims (pivot-mode ADC) and at
+# configuration 4's own shape, 768 dims in 96 chunks of 8 (per-query tables)
+IP_INDEXES = {
+    "ip96": (datagen.MixtureSpec("text", 8000, 96, 40, 0.1, center_scale=0.15, zipf=1.1, query_noise=0.05),
+             64, 32, 1000, True),
+    "ip768": (datagen.MixtureSpec("text", 3000, 768, 20, 0.1 * (96 / 768) ** 0.5, center_scale=768 ** -0.5,
+                                  zipf=1.1, query_noise=0.05), 64, 96, 400, True),
+}
+
+
 @pytest.fixture(scope="session")
 def index_root():
     d = os.environ.get("GANN_TEST_INDEX_DIR")
@@ -63,7 +75,7 @@ def get_index(root: str, name: str) -> dict:
     """Build (once) and return paths + queries of a named test index."""
     if name in _built:
         return _built[name]
-    spec, R, M, nav_s, nav = INDEXES[name]
+    spec, R, M, nav_s, nav = INDEXES[name] if name in INDEXES else IP_INDEXES[name]
     d = os.path.join(root, name)
     paths = formats.index_paths(d)
     dev = "cuda" if has_gpu() else "cpu"

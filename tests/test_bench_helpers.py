@@ -31,7 +31,33 @@ def test_traffic_scales_the_committed_capture_by_hops():
     assert b == base and "ef=176" in src
     b2, _ = bench.traffic_per_launch("c1", 10_000_000, 192, 2 * hops)
     assert b2 == 2 * base
-    assert bench.traffic_per_launch("c1", 123, 176, hops)[0] is None
+    # another point count of the same configuration: the nearest capture, named as such
+    b3, src3 = bench.traffic_per_launch("c1", 123, 176, hops)
+    assert b3 == base and "10000000-point" in src3
+    assert bench.traffic_per_launch("c9", 10_000_000, 176, hops)[0] is None
+
+
+def test_shards_cover_the_query_set():
+    for n in (0, 1, 7, 100_000):
+        for world in (1, 2, 3, 8):
+            parts = [bench.shard(n, r, world) for r in range(world)]
+            assert parts[0][0] == 0 and parts[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+
+
+def test_recall_table_merges_both_arms():
+    t = bench.recall_table([(16, 0.5), (24, 0.7)], {"oracle": [[16, 0.5], [24, 0.69]],
+                                                   "reference_gpu": [[16, 0.5, 9990]]})
+    assert t["rows"][1] == {"ef": 24, "ours": 0.7, "oracle": 0.69, "reference_gpu": None}
+    assert abs(t["max_abs_diff_oracle"] - 0.01) < 1e-9 and t["max_abs_diff_reference_gpu"] == 0.0
+    assert bench.recall_table([(16, 0.5)], None)["max_abs_diff_oracle"] is None
+
+
+def test_defaults_name_the_headline_configuration():
+    a = bench.parse([])
+    assert a.config == "c2" and a.nq == 100_000
+    efs = [int(x) for x in a.efs.split(",")]
+    assert efs == sorted(efs)
 
 
 def test_clock_samples_inside_the_window():

@@ -226,3 +226,27 @@ def test_part_calls_reject_bad_arguments():
     blob = b"\0" * api.PART_BLOB_BYTES
     assert api.lib.gann_part_export(None, None, 0) == api.GANN_EINVAL
     assert api.lib.gann_part_attach(None, 0, blob, len(blob)) == api.GANN_EINVAL
+
+
+def test_check_recall_tool(tmp_path):
+    """check_recall (bin/check_recall.cpp:11-32): recall of a bin result file
+    against an ivecs ground truth, and its errors."""
+    import subprocess
+    from gustann_b200 import build as nb
+    tool = nb.build_check()
+    gt = np.array([[1, 2, 3, 4], [5, 6, 7, 8], [9, 10, 11, 12]], np.int32)
+    formats.write_vecs(str(tmp_path / "gt.ivecs"), gt)
+    res = np.array([[2, 1, 0], [5, 5, 9], [0, 0, 0]], np.int32)
+    formats.write_bin(str(tmp_path / "out.bin"), res)
+    r = subprocess.run([tool, str(tmp_path / "out.bin"), str(tmp_path / "gt.ivecs")], capture_output=True, text=True)
+    assert r.returncode == 0
+    # row 0: {2,1} in top-3 {1,2,3}; row 1: 5 twice (each counts); row 2: none
+    assert r.stdout.strip() == f"Recall @ 3: {4 / 9:.6f}"
+    formats.write_bin(str(tmp_path / "short.bin"), res[:2])
+    r = subprocess.run([tool, str(tmp_path / "short.bin"), str(tmp_path / "gt.ivecs")], capture_output=True, text=True)
+    assert r.returncode != 0 and "NUM mismatch" in r.stdout
+    formats.write_bin(str(tmp_path / "wide.bin"), np.zeros((3, 5), np.int32))
+    r = subprocess.run([tool, str(tmp_path / "wide.bin"), str(tmp_path / "gt.ivecs")], capture_output=True, text=True)
+    assert r.returncode != 0 and "DIM mismatch" in r.stdout
+    r = subprocess.run([tool, str(tmp_path / "missing.bin"), str(tmp_path / "gt.ivecs")], capture_output=True, text=True)
+    assert r.returncode != 0

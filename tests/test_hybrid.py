@@ -166,3 +166,31 @@ def test_cli_hybrid_mode(index_root, tmp_path):
     assert b.returncode == 0, b.stderr
     rec = [float(ln.split()[-1]) for ln in b.stdout.splitlines() if ln.startswith("[REPORT] RECALL:")]
     assert rec and abs(rec[-1] - 1.0) < 1e-9, b.stdout
+
+
+@pytest.mark.gpu
+def test_cli_output_and_check_recall(index_root, tmp_path):
+    """search_mem --output writes the bin result file that check_recall
+    (bin/check_recall.cpp) scores; both report the same recall against an
+    exact ground truth made on the GPU (gann_exact_knn)."""
+    import torch
+    from gustann_b200 import build as nb
+    from gustann_b200.api import exact_knn
+    info = get_index(index_root, "u8")
+    p = info["paths"]
+    q = info["queries"][:200].astype(np.uint8)
+    qf, gf, of = tmp_path / "q.bvecs", tmp_path / "gt.ivecs", tmp_path / "out.bin"
+    formats.write_vecs(str(qf), q)
+    _, X, _, _ = formats.read_disk_index(p["index_file"], formats.UINT8)
+    ids, _ = exact_knn(torch.from_numpy(np.ascontiguousarray(X)).cuda(), torch.from_numpy(q).cuda(), 10)
+    formats.write_vecs(str(gf), ids.cpu().numpy())
+    cli = os.path.join(ROOT, "gustann_b200", "_lib", "search_mem")
+    r = subprocess.run([cli, "--query", str(qf), "--index", p["index_file"], "--pq_data", p["pq_file_prefix"],
+                        "--nav_graph", p["nav_graph_prefix"], "--ground_truth", str(gf), "--data_type", "uint8",
+                        "--topk", "10", "--ef_search", "40", "-R", "1", "-G", "--output", str(of)],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    rec = [float(ln.split()[-1]) for ln in r.stdout.splitlines() if ln.startswith("[REPORT] RECALL:")]
+    c = subprocess.run([nb.build_check(), str(of), str(gf)], capture_output=True, text=True)
+    assert c.returncode == 0, c.stdout + c.stderr
+    assert rec and c.stdout.strip() == f"Recall @ 10: {rec[-1]:.6f}" and rec[-1] > 0.5

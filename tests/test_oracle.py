@@ -100,3 +100,25 @@ def test_recall_improves_with_ef(index_root):
         nns = o.search(q, 10, ef)[0]
         recs.append(np.mean([len(set(a) & set(b)) for a, b in zip(nns, gt)]) / 10)
     assert recs[0] <= recs[1] <= recs[2] and recs[2] > 0.9, recs
+
+
+def test_ip_oracle_definitions():
+    """Inner product (no reference counterpart): table entries are
+    -(q . pivot) per chunk, exact distances -<q, x>, results ascending."""
+    p = formats.index_paths(os.path.join(GOLD, "g_f32"))
+    q = np.load(os.path.join(GOLD, "g_f32", "queries.npy"))[:16]
+    o = Oracle(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"], formats.FLOAT, metric=1)
+    piv, cen, offs, _ = formats.read_pq(p["pq_file_prefix"])
+    lut = o.lut(q[:4])
+    for c in range(len(offs) - 1):
+        a, b = offs[c], offs[c + 1]
+        exact = -(q[:4, None, a:b].astype(np.float64) * piv[None, :, a:b].astype(np.float64)).sum(-1)
+        np.testing.assert_allclose(lut[:, c, :], exact, rtol=1e-5, atol=1e-6)
+    nns, dist, found, hops, flags = o.search(q, 10, 40)
+    _, vec, _, _ = formats.read_disk_index(p["index_file"], formats.FLOAT)
+    assert np.all(np.diff(dist, axis=1) >= 0)
+    exact = -np.einsum("qd,qkd->qk", q.astype(np.float64), vec[nns].astype(np.float64))
+    np.testing.assert_allclose(dist, exact, rtol=1e-5, atol=1e-6)
+    # the L2 search of the same oracle differs (another metric, another order)
+    o2 = Oracle(p["index_file"], p["pq_file_prefix"], p["nav_graph_prefix"], formats.FLOAT)
+    assert not np.array_equal(o2.search(q, 10, 40)[1], dist)
