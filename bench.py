@@ -75,6 +75,8 @@ def parse(argv=None):
     ap.add_argument("--parity-queries", type=int, default=2000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true")
+    ap.add_argument("--adc-mode", type=int, default=0,
+                    help="GANN_OPT_ADC_MODE: 0 auto, 1 per-query tables, 2 resident pivot table, 3 filtered")
     ap.add_argument("--split-records", action="store_true",
                     help="N>1: each rank holds 1/N of the node records and reads the others over NVLink")
     a = ap.parse_args(argv)
@@ -464,6 +466,9 @@ def run_ours(args, d: Dist):
     else:
         g.init_pure_mem(cfg, True)
     t_open = time.time() - t0
+    if args.adc_mode:
+        from gustann_b200.api import GANN_OPT_ADC_MODE
+        g.set_option(GANN_OPT_ADC_MODE, args.adc_mode)
 
     # operating point: every rank sweeps the same first queries of the set, so
     # all choose the same ef; the sweep covers every ef of the list
@@ -567,7 +572,8 @@ def run_ours(args, d: Dist):
                "data": "synthetic", "config": config_json(args, spec, ef, round(rec, 5), passes), "e2e": e2e,
                "roofline": roof, "cpu_baseline": cpu, "clocks": ck, "gpu_launches": args.steps,
                "parity": parity, "timed_results_equal_untimed": same, "recall_sweep": table,
-               "index_build_s": meta.get("timings"), "index_load_s": round(t_open, 1)}
+               "index_build_s": meta.get("timings"), "index_load_s": round(t_open, 1),
+               "adc_mode": args.adc_mode}
     d.barrier()          # split records: peers read this rank's range until every rank is done
     g.close()
     return out

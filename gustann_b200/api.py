@@ -33,7 +33,7 @@ EXPORTS = ["gann_open", "gann_open_device", "gann_search", "gann_search_device",
            "gann_robust_prune", "gann_sort_unique_rows"]
 GANN_OPT_ADC_MODE, GANN_OPT_PIVOT_WARPS, GANN_OPT_NEIGHBOUR_CODES = 1, 2, 3
 LAYOUT_AUTO, LAYOUT_SEPARATE, LAYOUT_NEIGHBOUR_CODES = 0, 1, 2
-ADC_AUTO, ADC_TABLE, ADC_PIVOT = 0, 1, 2
+ADC_AUTO, ADC_TABLE, ADC_PIVOT, ADC_FILTERED = 0, 1, 2, 3
 METRIC_L2, METRIC_IP = 0, 1
 
 

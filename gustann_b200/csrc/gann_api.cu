@@ -822,9 +822,13 @@ int gann_set_option(gann_handle* h, int32_t option, int64_t value) {
   if (!h) return set_error(GANN_EINVAL, "gann_set_option: null handle");
   switch (option) {
     case GANN_OPT_ADC_MODE:
-      if (value < 0 || value > 2) return set_error(GANN_EINVAL, "gann_set_option: ADC mode must be 0, 1 or 2");
+      if (value < 0 || value > 3) return set_error(GANN_EINVAL, "gann_set_option: ADC mode must be 0, 1, 2 or 3");
       if (value == 2 && (h->ix.piv_width == 0 || h->ix.dim > 128))
         return set_error(GANN_EUNSUPPORTED, "gann_set_option: pivot mode needs <= 4 dims per chunk and dim <= 128");
+      if (value == 3 && (h->ix.piv_width == 0 || h->ix.dim > 128 || h->ix.chunks > 32 ||
+                         h->ix.metric != GANN_METRIC_L2))
+        return set_error(GANN_EUNSUPPORTED,
+                         "gann_set_option: filtered mode needs L2, <= 4 dims per chunk, <= 32 chunks and dim <= 128");
       h->ix.adc_mode = static_cast<int32_t>(value);
       return GANN_OK;
     case GANN_OPT_PIVOT_WARPS:

@@ -308,9 +308,112 @@ __device__ __forceinline__ float adc16_piv(float s, const uint4 c, const PivTab&
   return s;
 }
 
+// Table entry of chunk b for pivot row p: the reference's fp32 operations on
+// the chunk's residual dims (as adc16_piv); CW = 3 when every chunk has 3
+// dims, else 4 (zero padding contributes fma(0, 0, e) = e).
+template <int CW>
+__device__ __forceinline__ float piv_entry(const float4 q, const float4 p) {
+  float dx, dy;
+  asm("{.reg .b64 a, b, c;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "sub.rn.f32x2 c, a, b;\n\tmov.b64 {%0, %1}, c;}"
+      : "=f"(dx), "=f"(dy) : "f"(q.x), "f"(q.y), "f"(p.x), "f"(p.y));
+  float e = __fmul_rn(dx, dx);
+  e = __fmaf_rn(dy, dy, e);
+  float d = __fsub_rn(q.z, p.z);
+  e = __fmaf_rn(d, d, e);
+  if (CW > 3) {
+    d = __fsub_rn(q.w, p.w);
+    e = __fmaf_rn(d, d, e);
+  }
+  return e;
+}
+
+// Filtered mode: a per-query table of 8-bit lower bounds of the ADC table
+// entries, lb(b, j) = mn_b + q_bj * sc <= entry(b, j) (real arithmetic), so
+// that sum_b lb(b, code_b) = MN + sc * Q bounds the real sum of the entries of
+// a candidate from below with one integer Q; the reference's sequential fp32
+// sum of M non-negative entries is at least (1 - (M - 1) 2^-24) times the real
+// sum, which kLbSlack covers for M <= 128. A candidate whose bound exceeds a
+// full pool's last distance is cut by the reference's merge whatever its exact
+// value, so its exact ADC is not needed.
+constexpr float kLbSlack = 0.99999237060546875f;   // 1 - 2^-17
+struct FiltParams {
+  float sc = 1.f;       // quantisation step
+  float mnsum = 0.f;    // sum of the per-chunk minima, rounded down
+  float4 q = {0.f, 0.f, 0.f, 0.f};  // this lane's chunk residual (lane b = chunk b)
+};
+
+__device__ __forceinline__ float key_dist(uint64_t key) {
+  const uint32_t b = static_cast<uint32_t>(key >> 32);
+  return __uint_as_float((b & 0x80000000u) ? (b & 0x7fffffffu) : ~b);
+}
+
+// Sum of a candidate's 8-bit bounds over chunks 0..M-1 (integer, exact).
+__device__ __forceinline__ int lut8_sum(const uint8_t* __restrict__ lut8, const uint4 c0, const uint4 c1, int M) {
+  const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  int q = 0;
+  if (M == 32) {
+#pragma unroll
+    for (int b = 0; b < 32; ++b) q += lut8[b * kPivots + static_cast<int>(__byte_perm(w[b >> 2], 0u, 0x4440u | (b & 3)))];
+  } else {
+#pragma unroll
+    for (int b = 0; b < 32; ++b)
+      if (b < M) q += lut8[b * kPivots + static_cast<int>(__byte_perm(w[b >> 2], 0u, 0x4440u | (b & 3)))];
+  }
+  return q;
+}
+
+// Build the 8-bit bound table of one query from q - c (`qc`, shared memory)
+// and the pivot rows in global memory. The scale comes from chunk 0's range;
+// any positive scale keeps the bounds valid, as entries above 255 steps clamp
+// (a looser bound). Each stored step is checked with round-up arithmetic and
+// lowered until mn + q * sc <= entry holds exactly.
+template <int CW>
+__device__ void build_lut8(const DeviceIndex& ix, const float* __restrict__ qc, uint8_t* __restrict__ lut8, int lane,
+                           FiltParams& fp) {
+  float sc = 1.f, inv = 1.f, mnsum = 0.f;
+  for (int b = 0; b < ix.chunks; ++b) {
+    const int a0 = __ldg(ix.chunk_off + b), a1 = __ldg(ix.chunk_off + b + 1);
+    float r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = a0 + i < a1 ? qc[a0 + i] : 0.f;
+    const float4 q = make_float4(r[0], r[1], r[2], r[3]);
+    float e[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) e[t] = piv_entry<CW>(q, __ldg(ix.piv4 + b * kPivots + lane + kWarp * t));
+    float lo = e[0], hi = e[0];
+#pragma unroll
+    for (int t = 1; t < 8; ++t) {
+      lo = fminf(lo, e[t]);
+      hi = fmaxf(hi, e[t]);
+    }
+    // entries are >= +0, so their bit patterns order like the values
+    const float mn = __uint_as_float(__reduce_min_sync(kFull, __float_as_uint(lo)));
+    if (b == 0) {
+      const float mx = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(hi)));
+      sc = mx > mn ? __fmul_ru(__fsub_ru(mx, mn), 1.f / 255.f) : 1.f;
+      inv = 1.f / sc;
+    }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const float x = __fmul_rz(__fsub_rz(e[t], mn), inv);
+      int qv = x >= 255.f ? 255 : static_cast<int>(x);
+      while (qv > 0 && __fmaf_ru(static_cast<float>(qv), sc, mn) > e[t]) --qv;
+      lut8[b * kPivots + lane + kWarp * t] = static_cast<uint8_t>(qv);
+    }
+    mnsum = __fadd_rd(mnsum, mn);
+  }
+  fp.sc = sc;
+  fp.mnsum = mnsum;
+}
+
 struct WarpSmem {
   float* lut;     // per-query ADC table (table mode)
   float4* qcp;    // per-chunk query residuals, 4 dims padded (pivot mode)
+  uint8_t* lut8;  // per-query 8-bit lower-bound table [M x 256] (filtered mode)
+  float* ex;      // table entries of up to 8 candidates [8 x kExRow] (filtered mode)
+  const uint8_t** xrow;  // code rows of the candidates whose exact ADC runs (filtered mode)
+  float* xd;      // their exact ADC sums (filtered mode)
   float* qs;      // q, then q'' = (q - c) + c once the entry is known
   float* qc;      // q - c
   uint64_t* pool;  // up to ef keys, sorted
@@ -323,9 +426,17 @@ struct WarpSmem {
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
+// Row stride (floats) of the filtered mode's entry matrix: 16-byte aligned
+// rows that start 16 bytes apart in the banks, so 8 lanes reading a row each
+// with 16-byte loads do not conflict.
+constexpr int kExRow = 36;
+constexpr int kExGroup = 8;   // candidates whose entries are computed together
+
+enum CarveMode { kCarveTable = 0, kCarvePivot = 1, kCarveFilt = 2 };
+
 // Shared-memory carve-up of one warp; mirrored by search_smem_bytes().
 __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim, int npl, int pl,
-                                        int topk, WarpSmem* w, bool piv = false) {
+                                        int topk, WarpSmem* w, int mode = kCarveTable) {
   size_t off = 0;
   auto take = [&](size_t bytes) {
     unsigned char* p = base ? base + off : nullptr;
@@ -333,8 +444,12 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
     return p;
   };
   const int dpad = (dim + 3) & ~3;
-  unsigned char* lut = piv ? nullptr : take(sizeof(float) * chunks * kPivots);
-  unsigned char* qcp = piv ? take(sizeof(float4) * chunks) : nullptr;
+  unsigned char* lut = mode == kCarveTable ? take(sizeof(float) * chunks * kPivots) : nullptr;
+  unsigned char* qcp = mode == kCarvePivot ? take(sizeof(float4) * chunks) : nullptr;
+  unsigned char* lut8 = mode == kCarveFilt ? take(static_cast<size_t>(chunks) * kPivots) : nullptr;
+  unsigned char* ex = mode == kCarveFilt ? take(sizeof(float) * kExGroup * kExRow) : nullptr;
+  unsigned char* xrow = mode == kCarveFilt ? take(sizeof(void*) * npl * kWarp) : nullptr;
+  unsigned char* xd = mode == kCarveFilt ? take(sizeof(float) * npl * kWarp) : nullptr;
   unsigned char* qs = take(sizeof(float) * dpad);
   unsigned char* qc = take(sizeof(float) * dpad);
   unsigned char* pool = take(sizeof(uint64_t) * pl * kWarp);
@@ -346,6 +461,10 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
   if (w) {
     w->lut = reinterpret_cast<float*>(lut);
     w->qcp = reinterpret_cast<float4*>(qcp);
+    w->lut8 = lut8;
+    w->ex = reinterpret_cast<float*>(ex);
+    w->xrow = reinterpret_cast<const uint8_t**>(xrow);
+    w->xd = reinterpret_cast<float*>(xd);
     w->qs = reinterpret_cast<float*>(qs);
     w->qc = reinterpret_cast<float*>(qc);
     w->pool = reinterpret_cast<uint64_t*>(pool);
@@ -446,9 +565,9 @@ __global__ void gather_neighbour_codes(const uint32_t* __restrict__ adj, int adj
 // with at most 32 of them runs one ADC pass instead of NPL. (Without a table,
 // e.g. gann_search_noalloc, every neighbour is evaluated; duplicates of pool
 // entries are then dropped by the rank search.)
-template <typename T, int NPL, int VP, int PIV, bool IP>
+template <typename T, int NPL, int VP, int PIV, bool IP, bool FILT>
 __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid, uint32_t entry,
-                         const WarpSmem& s, const PivTab& piv, int lane, int pl) {
+                         const WarpSmem& s, const PivTab& piv, int lane, int pl, const FiltParams& fp) {
   const int dim = ix.dim, M = ix.chunks, L = a.ef, topk = a.topk;
   const int mw = ix.code_stride >> 4;
   int psize = 0, tcnt = 0, pfirst = 0;
@@ -533,12 +652,69 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     pfirst = ppos >= 0 ? ppos : psize;
     const uint64_t pstar = ppos >= 0 ? s.pool[ppos] : ~0ull;
 
-    // ADC of every neighbour not known to be in the pool, one lane per
-    // neighbour, chunks in order
+    // ADC of every neighbour not known to be in the pool, chunks in order
     float dsum[NPL];
 #pragma unroll
     for (int k = 0; k < NPL; ++k) dsum[k] = 0.f;
-    for (int w = 0; w < mw; ++w) {
+    if constexpr (FILT) {
+      // a full pool: candidates whose 8-bit bound exceeds its last distance
+      // are dropped without their exact ADC
+      if (psize == L) {
+        const float lastd = key_dist(s.pool[L - 1]);
+#pragma unroll
+        for (int k = 0; k < NPL; ++k) {
+          if (__any_sync(kFull, ok[k])) {
+            const int qsum = lut8_sum(s.lut8, c0[k], c1[k], M);
+            const float lb = __fmaf_rd(fp.sc, static_cast<float>(qsum), fp.mnsum);
+            if (ok[k] && __fmul_rd(lb, kLbSlack) > lastd) ok[k] = false;
+          }
+        }
+      }
+      // exact ADC of the rest: lane b computes chunk b's table entry of up to
+      // kExGroup candidates (the reference's fp32 operations on the pivot row),
+      // then one lane per candidate adds the entries in chunk order
+      int xpos[NPL];
+      int nx = 0;
+#pragma unroll
+      for (int k = 0; k < NPL; ++k) {
+        const unsigned bm = __ballot_sync(kFull, ok[k]);
+        xpos[k] = nx + __popc(bm & ((1u << lane) - 1u));
+        if (ok[k]) s.xrow[xpos[k]] = reinterpret_cast<const uint8_t*>(crow[k]);
+        nx += __popc(bm);
+      }
+      __syncwarp();
+      for (int g = 0; g < nx; g += kExGroup) {
+        const int gn = min(kExGroup, nx - g);
+        float4 pr[kExGroup];
+#pragma unroll
+        for (int c = 0; c < kExGroup; ++c) {
+          pr[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (c < gn && lane < M) pr[c] = __ldg(ix.piv4 + lane * kPivots + __ldg(s.xrow[g + c] + lane));
+        }
+#pragma unroll
+        for (int c = 0; c < kExGroup; ++c)
+          if (c < gn && lane < M) s.ex[c * kExRow + lane] = piv_entry<PIV>(fp.q, pr[c]);
+        __syncwarp();
+        if (lane < gn) {
+          const float4* row = reinterpret_cast<const float4*>(s.ex + lane * kExRow);
+          float acc = 0.f;
+          if (M == 32) {
+#pragma unroll
+            for (int b4 = 0; b4 < 8; ++b4) {
+              const float4 e = row[b4];
+              acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, e.x), e.y), e.z), e.w);
+            }
+          } else {
+            for (int b = 0; b < M; ++b) acc = __fadd_rn(acc, s.ex[lane * kExRow + b]);
+          }
+          s.xd[g + lane] = acc;
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int k = 0; k < NPL; ++k)
+        if (ok[k]) dsum[k] = s.xd[xpos[k]];
+    } else for (int w = 0; w < mw; ++w) {
       uint4 cur[NPL];
 #pragma unroll
       for (int k = 0; k < NPL; ++k)
@@ -579,7 +755,12 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       rk[k] = 0;
       if (ok[k] && (key[k] >> 1) >= last) ok[k] = false;
     }
-    if (psize > 0 && cnt > kWarp) {
+    // slots past the first only need a search when a lane still holds a live
+    // candidate there (after the drops above, rarely once the pool is full)
+    bool multi = false;
+#pragma unroll
+    for (int k = 1; k < NPL; ++k) multi = multi || __any_sync(kFull, ok[k]);
+    if (psize > 0 && multi) {
       for (int step = 1 << (31 - __clz(psize)); step > 0; step >>= 1) {
 #pragma unroll
         for (int k = 0; k < NPL; ++k) {
@@ -588,7 +769,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
         }
       }
     } else if (psize > 0) {
-      // at most 32 neighbours were evaluated: only the first pass holds any
+      // only the first slot holds live candidates
       for (int step = 1 << (31 - __clz(psize)); step > 0; step >>= 1) {
         const int t = rk[0] + step;
         if (ok[0] && t <= psize && (s.pool[t - 1] >> 1) < (key[0] >> 1)) rk[0] = t;
@@ -782,7 +963,7 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
 }
 
 // One query per warp, from query setup to the written top-k.
-template <typename T, int NPL, int VP, int PIV, bool IP>
+template <typename T, int NPL, int VP, int PIV, bool IP, bool FILT = false>
 __device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchArgs& a, const WarpSmem& s,
                                             const PivTab& piv, int lane, int pl) {
   const int dim = ix.dim;
@@ -814,7 +995,18 @@ __device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchA
       for (int i = lane; i < dim; i += kWarp) s.qs[i] = __fadd_rn(s.qc[i], __ldg(ix.centroid + i));
     // the table / pivot-mode query terms: q - c for L2, q for the inner product
     const float* qt = IP ? s.qs : s.qc;
-    if (PIV == 0) {
+    FiltParams fp;
+    if constexpr (FILT) {
+      // lane b keeps chunk b's residual dims; the 8-bit bound table
+      if (lane < ix.chunks) {
+        const int a0 = __ldg(ix.chunk_off + lane), a1 = __ldg(ix.chunk_off + lane + 1);
+        float r[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r[i] = a0 + i < a1 ? qt[a0 + i] : 0.f;
+        fp.q = make_float4(r[0], r[1], r[2], r[3]);
+      }
+      build_lut8<PIV>(ix, qt, s.lut8, lane, fp);
+    } else if (PIV == 0) {
       build_lut<IP>(ix, qt, s.lut, lane);
     } else {
       for (int c = lane; c < ix.chunks; c += kWarp) {
@@ -826,7 +1018,7 @@ __device__ __forceinline__ void run_queries(const DeviceIndex& ix, const SearchA
       }
     }
     __syncwarp();
-    traverse<T, NPL, VP, PIV, IP>(ix, a, qid, entry, s, piv, lane, pl);
+    traverse<T, NPL, VP, PIV, IP, FILT>(ix, a, qid, entry, s, piv, lane, pl, fp);
     __syncwarp();
   }
 }
@@ -836,7 +1028,7 @@ template <typename T, int NPL, int VP, bool IP>
 __global__ void __launch_bounds__(kWarp) search_kernel(const DeviceIndex ix, const SearchArgs a, int pl) {
   extern __shared__ __align__(16) unsigned char smem[];
   WarpSmem s;
-  carve(smem, ix.chunks, ix.dim, NPL, pl, a.topk, &s, false);
+  carve(smem, ix.chunks, ix.dim, NPL, pl, a.topk, &s, kCarveTable);
   run_queries<T, NPL, VP, 0, IP>(ix, a, s, PivTab{nullptr, nullptr, nullptr}, threadIdx.x, pl);
 }
 
@@ -871,8 +1063,22 @@ __global__ void __launch_bounds__(kWarp * piv_warps_max(NPL), 1) search_kernel_p
   __syncthreads();
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   WarpSmem s;
-  carve(smem + piv_tab_bytes(CW, ix.chunks) + per_warp * warp, ix.chunks, ix.dim, NPL, pl, a.topk, &s, true);
+  carve(smem + piv_tab_bytes(CW, ix.chunks) + per_warp * warp, ix.chunks, ix.dim, NPL, pl, a.topk, &s, kCarvePivot);
   run_queries<T, NPL, VP, CW, IP>(ix, a, s, piv, lane, pl);
+}
+
+// Filtered mode: no CTA-wide pivot table in shared memory; each warp keeps
+// its query's 8-bit bound table (M x 256 B) and reads the pivot rows of the
+// few candidates that need an exact ADC from global memory (L2-resident).
+constexpr int kFiltWarpsMax = 20;
+template <typename T, int NPL, int VP, int CW>
+__global__ void __launch_bounds__(kWarp * kFiltWarpsMax, 1) search_kernel_filt(const DeviceIndex ix, const SearchArgs a,
+                                                                               size_t per_warp, int pl) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  WarpSmem s;
+  carve(smem + per_warp * warp, ix.chunks, ix.dim, NPL, pl, a.topk, &s, kCarveFilt);
+  run_queries<T, NPL, VP, CW, false, true>(ix, a, s, PivTab{nullptr, nullptr, nullptr}, lane, pl);
 }
 
 template <bool IP>
@@ -922,11 +1128,27 @@ cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_co
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   const int pl = pl_for(a.ef);
+  if constexpr (VP == 4 && !IP) if (ix.piv_width > 0 && ix.chunks <= kWarp && ix.adc_mode == 3) {
+    // filtered mode: as many warps as their shared memory allows (<= 20)
+    const size_t per_warp = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, kCarveFilt);
+    int warps = static_cast<int>(std::min<size_t>(kFiltWarpsMax, optin / per_warp));
+    if (ix.piv_warps > 0) warps = std::min(warps, ix.piv_warps);
+    if (warps >= 8) {
+      const size_t smem = per_warp * warps;
+      auto fn = ix.piv_width == 3 ? search_kernel_filt<T, NPL, VP, 3> : search_kernel_filt<T, NPL, VP, 4>;
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      int64_t grid = std::min<int64_t>(sm_count, (a.nq + warps - 1) / warps);
+      if (grid <= 0) return cudaSuccess;
+      fn<<<static_cast<unsigned>(grid), kWarp * warps, smem, st>>>(ix, a, per_warp, pl);
+      return cudaGetLastError();
+    }
+  }
   if constexpr (VP == 4) if (ix.piv_width > 0 && ix.adc_mode != 1) {
     // pivot mode when the table plus at least 8 warps' state fit (dims <= 128;
     // wider vectors have too many chunks for a shared-memory pivot table)
     const size_t tab = piv_tab_bytes(ix.piv_width, ix.chunks);
-    const size_t per_warp = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, true);
+    const size_t per_warp = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, kCarvePivot);
     int warps = tab < static_cast<size_t>(optin)
                     ? static_cast<int>(std::min<size_t>(piv_warps_max(NPL), (optin - tab) / per_warp)) : 0;
     if (ix.piv_warps > 0) warps = std::min(warps, ix.piv_warps);
@@ -941,7 +1163,7 @@ cudaError_t launch_variant(const DeviceIndex& ix, const SearchArgs& a, int sm_co
       return cudaGetLastError();
     }
   }
-  const size_t smem = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, false);
+  const size_t smem = carve(nullptr, ix.chunks, ix.dim, NPL, pl, a.topk, nullptr, kCarveTable);
   auto fn = search_kernel<T, NPL, VP, IP>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -1061,25 +1283,41 @@ __global__ void __launch_bounds__(128) hop_step_kernel(const DeviceIndex ix, con
       if (lane == 0) atomicAdd(s.err + 2, 1);
       deg = deg < 0 ? 0 : R;
     }
-    // re-rank u on q'' and insert after every equal top-k entry (retset_push_32)
+    // re-rank u on q'' and insert after every equal top-k entry (retset_push_32):
+    // the insertion point counted with ballots, the tail moved by all lanes
     const float ex = warp_dist<T, IP>(s.qpp + qid * ix.dim, vec, ix.dim, lane);
-    if (lane == 0) {
+    {
       const int cnt = s.found[qid];
       int32_t* nn = s.nns + qid * s.topk;
       float* dd = s.dist + qid * s.topk;
       int le = 0;
-      while (le < cnt && dd[le] <= ex) ++le;
+      for (int t0 = 0; t0 < cnt; t0 += kWarp)
+        le += __popc(__ballot_sync(kFull, t0 + lane < cnt && dd[t0 + lane] <= ex));
       if (le < s.topk) {
-        for (int t = min(cnt, s.topk - 1); t > le; --t) {
-          dd[t] = dd[t - 1];
-          nn[t] = nn[t - 1];
+        const int hi = min(cnt, s.topk - 1);   // entries [le, hi) move one slot right
+        for (int c = (hi - le + kWarp - 1) / kWarp - 1; c >= 0; --c) {
+          const int t = le + c * kWarp + lane;
+          float dv = 0.f;
+          int iv = 0;
+          if (t < hi) {
+            dv = dd[t];
+            iv = nn[t];
+          }
+          __syncwarp();
+          if (t < hi) {
+            dd[t + 1] = dv;
+            nn[t + 1] = iv;
+          }
+          __syncwarp();
         }
-        dd[le] = ex;
-        nn[le] = u;
+        if (lane == 0) {
+          dd[le] = ex;
+          nn[le] = u;
+        }
       }
-      s.found[qid] = min(cnt + 1, s.topk);
+      if (lane == 0) s.found[qid] = min(cnt + 1, s.topk);
     }
-    // ADC of the neighbours, chunks in order
+    // ADC of the neighbours, chunks in order; code rows read 16 bytes at a time
     const float* lut = s.lut + qid * M * kPivots;
     for (int e = lane; e < deg; e += kWarp) {
       const uint32_t v = nbr[1 + e];
@@ -1088,9 +1326,9 @@ __global__ void __launch_bounds__(128) hop_step_kernel(const DeviceIndex ix, con
         nk[e] = ~0ull;
         continue;
       }
-      const uint8_t* code = ix.codes + static_cast<size_t>(v) * ix.code_stride;
+      const uint4* code = reinterpret_cast<const uint4*>(ix.codes + static_cast<size_t>(v) * ix.code_stride);
       float d = 0.f;
-      for (int j = 0; j < M; ++j) d = __fadd_rn(d, lut[j * kPivots + code[j]]);
+      for (int w = 0; w * 16 < M; ++w) d = adc16(d, __ldg(code + w), lut + 16 * w * kPivots, min(16, M - 16 * w));
       nk[e] = make_key(d, v);
     }
     __syncwarp();

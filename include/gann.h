@@ -281,9 +281,14 @@ int gann_close(gann_handle* h);
 /* Tuning options (no counterpart in the reference).
  *   GANN_OPT_ADC_MODE: 0 auto, 1 per-query ADC table in shared memory, 2 the
  *     PQ pivot table resident once per SM with table entries recomputed per
- *     lookup (bit-identical sums; needs <= 4 dims per chunk and D <= 128).
+ *     lookup (bit-identical sums; needs <= 4 dims per chunk and D <= 128),
+ *     3 filtered: a per-query table of 8-bit lower bounds of the entries
+ *     rejects the candidates a full pool would cut anyway, and only the rest
+ *     get their exact ADC, recomputed from the pivot rows (bit-identical
+ *     results; L2, <= 4 dims per chunk, <= 32 chunks, D <= 128).
  *     Auto picks 2 when it fits.
- *   GANN_OPT_PIVOT_WARPS: queries in flight per SM in mode 2 (8..24, 0 auto).
+ *   GANN_OPT_PIVOT_WARPS: queries in flight per SM in modes 2 and 3 (8..24,
+ *     0 auto).
  *   GANN_OPT_NEIGHBOUR_CODES: 1 read neighbour codes from the per-node copy
  *     when the handle has one (layout 0/2), 0 from the shared code array. */
 enum { GANN_OPT_ADC_MODE = 1, GANN_OPT_PIVOT_WARPS = 2, GANN_OPT_NEIGHBOUR_CODES = 3 };
