@@ -446,16 +446,37 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
   const int dpad = (dim + 3) & ~3;
   unsigned char* lut = mode == kCarveTable ? take(sizeof(float) * chunks * kPivots) : nullptr;
   unsigned char* qcp = mode == kCarvePivot ? take(sizeof(float4) * chunks) : nullptr;
-  unsigned char* lut8 = mode == kCarveFilt ? take(static_cast<size_t>(chunks) * kPivots) : nullptr;
-  unsigned char* ex = mode == kCarveFilt ? take(sizeof(float) * kExGroup * kExRow) : nullptr;
-  unsigned char* xrow = mode == kCarveFilt ? take(sizeof(void*) * npl * kWarp) : nullptr;
-  unsigned char* xd = mode == kCarveFilt ? take(sizeof(float) * npl * kWarp) : nullptr;
-  unsigned char* qs = take(sizeof(float) * dpad);
-  unsigned char* qc = take(sizeof(float) * dpad);
+  unsigned char *lut8 = nullptr, *ex = nullptr, *xrow = nullptr, *xd = nullptr;
+  unsigned char *qs, *qc, *cand, *candr, *hist;
+  if (mode == kCarveFilt) {
+    // the filtered mode's phases never overlap within a warp, so one region
+    // holds in turn the query (setup: qs, qc), a hop's compacted neighbours
+    // (candr, hist), the exact-ADC staging (ex, xrow, xd) and the merge
+    // buffers (cand, candr, hist); __syncwarp separates the phases
+    lut8 = take(static_cast<size_t>(chunks) * kPivots);
+    const size_t a_ex = align16(sizeof(float) * kExGroup * kExRow), a_xr = align16(sizeof(void*) * npl * kWarp);
+    const size_t a_xd = align16(sizeof(float) * npl * kWarp), a_q = align16(sizeof(float) * dpad);
+    const size_t a_c = align16(sizeof(uint64_t) * npl * kWarp), a_r = align16(sizeof(int) * npl * kWarp);
+    size_t bytes = a_ex + a_xr + a_xd;
+    bytes = bytes > 2 * a_q ? bytes : 2 * a_q;
+    bytes = bytes > a_c + 2 * a_r ? bytes : a_c + 2 * a_r;
+    unsigned char* reg = take(bytes);
+    ex = reg;
+    xrow = reg ? reg + a_ex : nullptr;
+    xd = reg ? reg + a_ex + a_xr : nullptr;
+    qs = reg;
+    qc = reg ? reg + a_q : nullptr;
+    cand = reg;
+    candr = reg ? reg + a_c : nullptr;
+    hist = reg ? reg + a_c + a_r : nullptr;
+  } else {
+    qs = take(sizeof(float) * dpad);
+    qc = take(sizeof(float) * dpad);
+    cand = take(sizeof(uint64_t) * npl * kWarp);
+    candr = take(sizeof(int) * npl * kWarp);
+    hist = take(sizeof(int) * npl * kWarp);
+  }
   unsigned char* pool = take(sizeof(uint64_t) * pl * kWarp);
-  unsigned char* cand = take(sizeof(uint64_t) * npl * kWarp);
-  unsigned char* candr = take(sizeof(int) * npl * kWarp);
-  unsigned char* hist = take(sizeof(int) * npl * kWarp);
   unsigned char* topd = take(sizeof(float) * topk);
   unsigned char* topi = take(sizeof(int) * topk);
   if (w) {

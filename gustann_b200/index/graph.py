@@ -254,17 +254,24 @@ def repair_connectivity(X: torch.Tensor, adj: torch.Tensor, entry: int, rounds: 
         else:
             near, _ = knn_exact(Xr, Xu, 1)
         del Xr, Xu
-        src = rs[near[:, 0]]
-        # one new edge per source node per round keeps the replacement local
-        order = torch.argsort(src, stable=True)
-        src, dst = src[order], un[order]
-        first = torch.ones_like(src, dtype=torch.bool)
-        first[1:] = src[1:] != src[:-1]
-        src, dst = src[first], dst[first]
-        deg = (adj[src] >= 0).sum(1)
-        slot = torch.where(deg < R, deg, torch.full_like(deg, R - 1))
-        adj[src, slot] = dst.to(adj.dtype)
+        attach_edges(adj, R, rs[near[:, 0]], un)
     return adj
+
+
+def attach_edges(adj: torch.Tensor, R: int, src: torch.Tensor, dst: torch.Tensor) -> None:
+    """Give node src[i] an edge to dst[i], in its first free slot or, if it has
+    none, over its last (farthest) edge; one new edge per source node per call
+    (the first listed), which keeps each replacement local."""
+    ok = src >= 0
+    src, dst = src[ok], dst[ok]
+    order = torch.argsort(src, stable=True)
+    src, dst = src[order], dst[order]
+    first = torch.ones_like(src, dtype=torch.bool)
+    first[1:] = src[1:] != src[:-1]
+    src, dst = src[first], dst[first]
+    deg = (adj[src, :R] >= 0).sum(1)
+    slot = torch.where(deg < R, deg, torch.full_like(deg, R - 1))
+    adj[src, slot] = dst.to(adj.dtype)
 
 
 def build_graph(X: torch.Tensor, R: int, alpha: float = 1.2, k: int | None = None,

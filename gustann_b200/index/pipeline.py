@@ -51,7 +51,6 @@ def build_index(root: str, X: torch.Tensor, dtype: int, R: int = 64, alpha: floa
     "auto" (vamana when ``X`` is on a GPU). Returns the path dict of
     :func:`gustann_b200.formats.index_paths` plus timings.
     """
-    from .graph import repair_connectivity
     os.makedirs(root, exist_ok=True)
     paths = formats.index_paths(root)
     t = {}
@@ -69,8 +68,7 @@ def build_index(root: str, X: torch.Tensor, dtype: int, R: int = 64, alpha: floa
             from .vamana import vamana_graph
             a, d, m = vamana_graph(Xg, codes_g, pivots, centroid, offs, R=R_g, L=L_g, alpha=alpha,
                                    passes=passes, seed=seed_g, verbose=verbose)
-            a = repair_connectivity(Xg, a, m, inplace=True)
-            return a, (a >= 0).sum(1).to(torch.int32), m
+            return a, d, m
         a, d = build_graph(Xg, R_g, alpha=alpha, seed=seed_g, long_range=long_range)
         return a, d, medoid(Xg)
 

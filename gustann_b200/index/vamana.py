@@ -22,7 +22,7 @@ import time
 import numpy as np
 import torch
 
-from .graph import _f32, medoid
+from .graph import _f32, attach_edges, medoid, reachable
 
 
 def _pad_rows(t: torch.Tensor, mult_bytes: int = 16) -> torch.Tensor:
@@ -138,6 +138,26 @@ def vamana_graph(X: torch.Tensor, codes: np.ndarray, pivots: np.ndarray, centroi
                 deg = (adj[:, :R] >= 0).sum(1).float()
                 print(f"[vamana] pass {pi} alpha={a}: {time.time() - t0:.1f}s, mean degree {float(deg.mean()):.1f}",
                       flush=True)
+        # connectivity: a search from the medoid only expands reachable nodes,
+        # so its best node for an unreachable point is a reachable node near
+        # it, which gets an edge to that point (one new edge per node a round)
+        for rnd in range(64):
+            seen = reachable(adj[:, :R], med)
+            if bool(seen.all()):
+                break
+            un = torch.nonzero(~seen).reshape(-1)
+            if verbose:
+                print(f"[vamana] repair round {rnd}: {un.numel()} unreachable", flush=True)
+            for s0 in range(0, un.numel(), maxb):
+                u = un[s0: s0 + maxb]
+                b = u.shape[0]
+                q = _f32(X[u]).contiguous()
+                nns = torch.empty((b, 1), dtype=torch.int32, device=dev)
+                dst = torch.empty((b, 1), dtype=torch.float32, device=dev)
+                fnd = torch.empty(b, dtype=torch.int32, device=dev)
+                g.search_device(q.data_ptr(), b, 1, L, nns.data_ptr(), dst.data_ptr(), fnd.data_ptr(), 0,
+                                stream.cuda_stream)
+                attach_edges(adj, R, nns[:, 0].long(), u)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = old_tf32
         g.close()
