@@ -366,12 +366,13 @@ __device__ __forceinline__ int lut8_sum(const uint8_t* __restrict__ lut8, const 
 // Build the 8-bit bound table of one query from q - c (`qc`, shared memory)
 // and the pivot rows in global memory. The scale comes from chunk 0's range;
 // any positive scale keeps the bounds valid, as entries above 255 steps clamp
-// (a looser bound). Each stored step is checked with round-up arithmetic and
-// lowered until mn + q * sc <= entry holds exactly.
+// (a looser bound). A step is (entry - mn) / sc evaluated with every operation
+// rounded toward zero on non-negative values, so it never exceeds the real
+// quotient, and its integer part q satisfies mn + q * sc <= entry exactly.
 template <int CW>
 __device__ void build_lut8(const DeviceIndex& ix, const float* __restrict__ qc, uint8_t* __restrict__ lut8, int lane,
                            FiltParams& fp) {
-  float sc = 1.f, inv = 1.f, mnsum = 0.f;
+  float sc = 1.f, inv = 1.f, mnsum = 0.f;   // inv <= 1 / sc
   for (int b = 0; b < ix.chunks; ++b) {
     const int a0 = __ldg(ix.chunk_off + b), a1 = __ldg(ix.chunk_off + b + 1);
     float r[4];
@@ -392,14 +393,12 @@ __device__ void build_lut8(const DeviceIndex& ix, const float* __restrict__ qc, 
     if (b == 0) {
       const float mx = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(hi)));
       sc = mx > mn ? __fmul_ru(__fsub_ru(mx, mn), 1.f / 255.f) : 1.f;
-      inv = 1.f / sc;
+      inv = __frcp_rz(sc);
     }
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
       const float x = __fmul_rz(__fsub_rz(e[t], mn), inv);
-      int qv = x >= 255.f ? 255 : static_cast<int>(x);
-      while (qv > 0 && __fmaf_ru(static_cast<float>(qv), sc, mn) > e[t]) --qv;
-      lut8[b * kPivots + lane + kWarp * t] = static_cast<uint8_t>(qv);
+      lut8[b * kPivots + lane + kWarp * t] = static_cast<uint8_t>(x >= 255.f ? 255 : static_cast<int>(x));
     }
     mnsum = __fadd_rd(mnsum, mn);
   }
@@ -682,12 +681,24 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
       // are dropped without their exact ADC
       if (psize == L) {
         const float lastd = key_dist(s.pool[L - 1]);
+        // first slot: one lane per candidate, 32 byte lookups each
+        if (__any_sync(kFull, ok[0])) {
+          const int qsum = lut8_sum(s.lut8, c0[0], c1[0], M);
+          const float lb = __fmaf_rd(fp.sc, static_cast<float>(qsum), fp.mnsum);
+          if (ok[0] && __fmul_rd(lb, kLbSlack) > lastd) ok[0] = false;
+        }
+        // later slots hold few candidates: the warp sums each one's bounds,
+        // lane b looking up chunk b (integer sums, exact in any order)
 #pragma unroll
-        for (int k = 0; k < NPL; ++k) {
-          if (__any_sync(kFull, ok[k])) {
-            const int qsum = lut8_sum(s.lut8, c0[k], c1[k], M);
+        for (int k = 1; k < NPL; ++k) {
+          for (unsigned m = __ballot_sync(kFull, ok[k]); m; m &= m - 1) {
+            const int src = __ffs(m) - 1;
+            const uint8_t* row = reinterpret_cast<const uint8_t*>(
+                __shfl_sync(kFull, reinterpret_cast<unsigned long long>(crow[k]), src));
+            const unsigned v = lane < M ? s.lut8[lane * kPivots + __ldg(row + lane)] : 0u;
+            const unsigned qsum = __reduce_add_sync(kFull, v);
             const float lb = __fmaf_rd(fp.sc, static_cast<float>(qsum), fp.mnsum);
-            if (ok[k] && __fmul_rd(lb, kLbSlack) > lastd) ok[k] = false;
+            if (lane == src && __fmul_rd(lb, kLbSlack) > lastd) ok[k] = false;
           }
         }
       }

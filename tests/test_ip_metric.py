@@ -34,7 +34,13 @@ def test_ip_lut_and_entry_bit_exact(index_root, name):
     q = info["queries"][:64]
     lut = g.probe_lut(q)
     np.testing.assert_array_equal(lut, o.lut(q))
-    assert (lut <= 0).mean() > 0.5          # -(q . p): mostly non-positive for nearby pivots
+    # entries are -(q . pivot) over each chunk's dims
+    from gustann_b200 import formats
+    piv, _, offs, _ = formats.read_pq(info["paths"]["pq_file_prefix"])
+    for c in (0, len(offs) // 2, len(offs) - 2):
+        a, b = int(offs[c]), int(offs[c + 1])
+        ref = -(q[:, None, a:b].astype(np.float64) * piv[None, :, a:b].astype(np.float64)).sum(-1)
+        np.testing.assert_allclose(lut[:, c, :], ref, rtol=1e-4, atol=1e-6)
     s, e = g.probe_entry(q)
     os_, oe, _ = o.nav(q)
     np.testing.assert_array_equal(s, os_)
