@@ -51,8 +51,8 @@ DEFAULTS = {
     "c0": dict(nq=10_000, efs="20,24,28,32,40,48,56,64,80,96,112,128,160,192,256"),
     "c1": dict(nq=10_000, efs="32,48,64,80,96,112,128,136,144,152,160,168,176,184,192,200,208,224,240,256,288,320,"
                               "384,448,512,640,768,1024"),
-    "c2": dict(nq=100_000, efs="16,20,24,28,32,36,40,44,48,56,64,72,80,88,96,104,112,128,144,160,192,224,256,320,"
-                               "384,512"),
+    "c2": dict(nq=100_000, efs="32,48,64,96,128,160,192,224,256,288,320,336,352,368,384,400,416,432,448,464,"
+                               "480,496,512,576,640,768,1024"),
 }
 RECALL_QUERIES = 10_000   # queries whose recall chooses the operating point (the first of the set)
 T_START = time.time()

@@ -447,15 +447,25 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
   unsigned char* qcp = mode == kCarvePivot ? take(sizeof(float4) * chunks) : nullptr;
   unsigned char *lut8 = nullptr, *ex = nullptr, *xrow = nullptr, *xd = nullptr;
   unsigned char *qs, *qc, *cand, *candr, *hist;
-  if (mode == kCarveFilt) {
+  const size_t a_q = align16(sizeof(float) * dpad);
+  const size_t a_c = align16(sizeof(uint64_t) * npl * kWarp), a_r = align16(sizeof(int) * npl * kWarp);
+  if (mode != kCarveFilt) {
+    // query setup (qs, qc) and the hop buffers (cand, candr, hist) are never
+    // live at once in a warp: qs is read into registers before the first hop
+    unsigned char* reg = take(2 * a_q > a_c + 2 * a_r ? 2 * a_q : a_c + 2 * a_r);
+    qs = reg;
+    qc = reg ? reg + a_q : nullptr;
+    cand = reg;
+    candr = reg ? reg + a_c : nullptr;
+    hist = reg ? reg + a_c + a_r : nullptr;
+  } else {
     // the filtered mode's phases never overlap within a warp, so one region
     // holds in turn the query (setup: qs, qc), a hop's compacted neighbours
     // (candr, hist), the exact-ADC staging (ex, xrow, xd) and the merge
     // buffers (cand, candr, hist); __syncwarp separates the phases
     lut8 = take(static_cast<size_t>(chunks) * kPivots);
     const size_t a_ex = align16(sizeof(float) * kExGroup * kExRow), a_xr = align16(sizeof(void*) * npl * kWarp);
-    const size_t a_xd = align16(sizeof(float) * npl * kWarp), a_q = align16(sizeof(float) * dpad);
-    const size_t a_c = align16(sizeof(uint64_t) * npl * kWarp), a_r = align16(sizeof(int) * npl * kWarp);
+    const size_t a_xd = align16(sizeof(float) * npl * kWarp);
     size_t bytes = a_ex + a_xr + a_xd;
     bytes = bytes > 2 * a_q ? bytes : 2 * a_q;
     bytes = bytes > a_c + 2 * a_r ? bytes : a_c + 2 * a_r;
@@ -468,12 +478,6 @@ __host__ __device__ inline size_t carve(unsigned char* base, int chunks, int dim
     cand = reg;
     candr = reg ? reg + a_c : nullptr;
     hist = reg ? reg + a_c + a_r : nullptr;
-  } else {
-    qs = take(sizeof(float) * dpad);
-    qc = take(sizeof(float) * dpad);
-    cand = take(sizeof(uint64_t) * npl * kWarp);
-    candr = take(sizeof(int) * npl * kWarp);
-    hist = take(sizeof(int) * npl * kWarp);
   }
   unsigned char* pool = take(sizeof(uint64_t) * pl * kWarp);
   unsigned char* topd = take(sizeof(float) * topk);
@@ -911,20 +915,35 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
           rmin = min(rmin, cr[k]);
         }
       }
+      int rmax = 0;
+#pragma unroll
+      for (int k = 0; k < NPL; ++k)
+        if (lane + kWarp * k < S) rmax = max(rmax, cr[k]);
       rmin = __reduce_min_sync(kFull, rmin);
+      rmax = static_cast<int>(__reduce_max_sync(kFull, static_cast<unsigned>(rmax)));
       // survivor ranks in key order are non-decreasing: hist[t] = rank of the
       // t-th smallest survivor; entry i >= rmin moves right by #{t : hist[t] <= i}
 #pragma unroll
       for (int k = 0; k < NPL; ++k)
         if (lane + kWarp * k < S) s.hist[cpos[k] - cr[k]] = cr[k];
       __syncwarp();
-      // moves, four chunks at a time from the last one down (an entry only moves
-      // right); entries pushed past `ef` leave the pool.
-      // The shift of entry i is an upper bound in hist, found by power-of-two
-      // steps with the four chunks' searches interleaved.
+      // moves, from the last chunk down (an entry only moves right); entries
+      // pushed past `ef` leave the pool. Chunks at or after the largest
+      // survivor rank move by S as a whole (every survivor ranks before them);
+      // the chunks from rmin up to there take each entry's shift, an upper bound
+      // in hist, found by power-of-two steps with four chunks interleaved.
       const int j0 = rmin >> 5;
+      const int ju = (rmax + kWarp - 1) >> 5;
+      for (int j = min((psize - 1) >> 5, (L - 1 - S) >> 5); j >= ju && j >= j0; --j) {
+        const int i = lane + kWarp * j;
+        uint64_t v = i < psize ? s.pool[i] : 0;
+        if (v == nxt) v &= ~1ull;
+        __syncwarp();
+        if (i < psize && i + S < L) s.pool[i + S] = v;
+      }
+      __syncwarp();
       const int sstep = 1 << (31 - __clz(S));
-      for (int jg = (psize - 1) >> 5; jg >= j0; jg -= 4) {
+      for (int jg = min((psize - 1) >> 5, ju - 1); jg >= j0; jg -= 4) {
         uint64_t v[4];
         int dst[4], sh[4];
         bool act[4];

@@ -261,9 +261,13 @@ def repair_connectivity(X: torch.Tensor, adj: torch.Tensor, entry: int, rounds: 
 def attach_edges(adj: torch.Tensor, R: int, src: torch.Tensor, dst: torch.Tensor) -> None:
     """Give node src[i] an edge to dst[i], in its first free slot or, if it has
     none, over its last (farthest) edge; one new edge per source node per call
-    (the first listed), which keeps each replacement local."""
+    (the first listed), which keeps each replacement local. An edge a row
+    already holds is not added again (a node listed as unreachable can have
+    become reachable since, through edges attached earlier in the same round)."""
     ok = src >= 0
     src, dst = src[ok], dst[ok]
+    fresh = ~(adj[src, :R] == dst[:, None].to(adj.dtype)).any(1)
+    src, dst = src[fresh], dst[fresh]
     order = torch.argsort(src, stable=True)
     src, dst = src[order], dst[order]
     first = torch.ones_like(src, dtype=torch.bool)

@@ -139,8 +139,12 @@ def vamana_graph(X: torch.Tensor, codes: np.ndarray, pivots: np.ndarray, centroi
                 print(f"[vamana] pass {pi} alpha={a}: {time.time() - t0:.1f}s, mean degree {float(deg.mean()):.1f}",
                       flush=True)
         # connectivity: a search from the medoid only expands reachable nodes,
-        # so its best node for an unreachable point is a reachable node near
-        # it, which gets an edge to that point (one new edge per node a round)
+        # so its nearest results for an unreachable point are reachable nodes
+        # near it; the nearest with a free slot gets an edge to the point (one
+        # new edge per node a round; a full row's last edge is replaced only
+        # when none of the candidates has room, since that can cut off another
+        # node)
+        cands = 16
         for rnd in range(64):
             seen = reachable(adj[:, :R], med)
             if bool(seen.all()):
@@ -152,12 +156,18 @@ def vamana_graph(X: torch.Tensor, codes: np.ndarray, pivots: np.ndarray, centroi
                 u = un[s0: s0 + maxb]
                 b = u.shape[0]
                 q = _f32(X[u]).contiguous()
-                nns = torch.empty((b, 1), dtype=torch.int32, device=dev)
-                dst = torch.empty((b, 1), dtype=torch.float32, device=dev)
+                k = min(cands, L)
+                nns = torch.empty((b, k), dtype=torch.int32, device=dev)
+                dst = torch.empty((b, k), dtype=torch.float32, device=dev)
                 fnd = torch.empty(b, dtype=torch.int32, device=dev)
-                g.search_device(q.data_ptr(), b, 1, L, nns.data_ptr(), dst.data_ptr(), fnd.data_ptr(), 0,
+                g.search_device(q.data_ptr(), b, k, L, nns.data_ptr(), dst.data_ptr(), fnd.data_ptr(), 0,
                                 stream.cuda_stream)
-                attach_edges(adj, R, nns[:, 0].long(), u)
+                c = nns.long()
+                valid = ar[None, :k] < fnd[:, None]
+                room = valid & ((adj[c.clamp_min(0), :R] >= 0).sum(-1) < R)
+                pick = torch.where(room.any(1), room.int().argmax(1), torch.zeros_like(fnd).long())
+                src = torch.where(fnd > 0, c.gather(1, pick[:, None])[:, 0], torch.full_like(pick, -1))
+                attach_edges(adj, R, src, u)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = old_tf32
         g.close()

@@ -39,6 +39,8 @@ def pytest_collection_modifyitems(config, items):
 # name -> (mixture spec, R, M, nav samples, nav?)
 INDEXES = {
     "u8": (datagen.MixtureSpec("sift", 12000, 128, 60, 20.0), 32, 32, 1500, True),
+    # configurations 0/2/3's shape: uint8, 128 dims, R = 64, M = 32 (4 dims a chunk)
+    "u8_r64": (datagen.MixtureSpec("sift", 16000, 128, 80, 20.0), 64, 32, 2000, True),
     "f32": (datagen.MixtureSpec("deep", 12000, 96, 60, 0.1, center_scale=0.15), 64, 32, 1500, True),
     "f32_odd": (datagen.MixtureSpec("deep", 4000, 40, 20, 0.1, center_scale=0.15), 96, 12, 500, True),
     "u8_nonav": (datagen.MixtureSpec("sift", 6000, 64, 30, 20.0), 48, 16, 0, False),

@@ -96,3 +96,15 @@ def test_pivot_sample_sorted_unique():
     from gustann_b200.index.pipeline import sample_pivots
     s = sample_pivots(10000, 1000)
     assert len(np.unique(s)) == 1000 and np.all(np.diff(s) > 0)
+
+
+def test_attach_edges_never_duplicates():
+    """attach_edges: one edge per source, free slot first, never an edge the
+    row already holds."""
+    import torch
+    from gustann_b200.index.graph import attach_edges
+    adj = torch.tensor([[1, 2, -1, -1], [0, 2, 3, 4], [0, -1, -1, -1]], dtype=torch.int32)
+    attach_edges(adj, 4, torch.tensor([0, 0, 1, 2]), torch.tensor([2, 3, 5, 0]))
+    # row 0: 2 already there, so its next offer (3) fills the free slot; row 1
+    # is full and takes 5 over its last edge; row 2 already holds 0
+    assert adj.tolist() == [[1, 2, 3, -1], [0, 2, 3, 5], [0, -1, -1, -1]]

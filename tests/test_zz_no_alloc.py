@@ -6,7 +6,9 @@ synchronisation is not acceptable mid-flight): the index arrays, queries and
 outputs are theirs, and the library's own per-call device state lives in a
 static device array. Its results must equal those of the existing entry point
 (gann_open_device + gann_search_device) over the same arrays, bit for bit, on
-consecutive calls -- the second call also proves the shared scratch is reset.
+consecutive calls -- the second call also proves the shared scratch is reset --
+and those of the CPU oracle entered at the same node (the medoid: this
+descriptor has no pivot graph).
 
 This file is collected last on purpose, and passes alone or after the others.
 """
@@ -42,7 +44,7 @@ def _device_index(name):
     t = {"vec": torch.from_numpy(v).cuda()[:, : vec.shape[1]], "adj": torch.from_numpy(a).cuda(),
          "codes": torch.from_numpy(c).cuda()}
     q = np.load(os.path.join(ROOT, "tests", "golden", name, "queries.npy"))
-    return t, pivots, centroid, offs, lay, q
+    return t, pivots, centroid, offs, lay, q, p
 
 
 def _descriptor(api, t, pivots, centroid, offs, lay):
@@ -62,7 +64,11 @@ def _descriptor(api, t, pivots, centroid, offs, lay):
 def test_noalloc_matches_existing_entry_point(name):
     import torch
     from gustann_b200 import api
-    t, pivots, centroid, offs, lay, q = _device_index(name)
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle
+    t, pivots, centroid, offs, lay, q, paths = _device_index(name)
+    o = Oracle(paths["index_file"], paths["pq_file_prefix"], "", GOLD[name])
     dq = torch.from_numpy(q).cuda()
     nq = len(q)
     stream = torch.cuda.current_stream()
@@ -79,16 +85,25 @@ def test_noalloc_matches_existing_entry_point(name):
                     g.search_device(dq.data_ptr(), nq, topk, ef, nns.data_ptr(), dst.data_ptr(), fnd.data_ptr(), 0,
                                     stream.cuda_stream)
                 else:
+                    dev_before = torch.cuda.current_device()
                     rc = api.lib.gann_search_noalloc(C.byref(desc), dq.data_ptr(), nq, topk, ef, nns.data_ptr(),
                                                      dst.data_ptr(), fnd.data_ptr(), stream.cuda_stream)
                     assert rc == api.GANN_OK, api.lib.gann_last_error()
+                    assert torch.cuda.current_device() == dev_before
                 torch.cuda.synchronize()
                 outs.append((nns.cpu().numpy(), dst.cpu().numpy(), fnd.cpu().numpy()))
             for a, b in zip(*outs):
                 np.testing.assert_array_equal(a, b)
             assert (outs[1][2] == topk).all()
+            onns, odist, ofound, _, flags = o.search(q, topk, ef, entries=np.full(nq, lay.medoid, np.int32))
+            ok = flags == 0
+            assert ok.mean() > 0.9
+            np.testing.assert_array_equal(outs[1][0][ok], onns[ok])
+            np.testing.assert_array_equal(outs[1][1][ok], odist[ok])
+            np.testing.assert_array_equal(outs[1][2][ok], ofound[ok])
     finally:
         g.close()
+        o.close()
 
 
 def test_noalloc_rejects_oversized_index():
