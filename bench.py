@@ -53,6 +53,7 @@ DEFAULTS = {
                               "384,448,512,640,768,1024"),
     "c2": dict(nq=100_000, efs="32,48,64,96,128,160,192,224,256,288,320,336,352,368,384,400,416,432,448,464,"
                                "480,496,512,576,640,768,1024"),
+    "c4": dict(nq=10_000, topk=100, efs="100,112,128,144,160,176,192,224,256,288,320,384,448,512,640,768,1024"),
 }
 RECALL_QUERIES = 10_000   # queries whose recall chooses the operating point (the first of the set)
 T_START = time.time()
@@ -81,6 +82,10 @@ def parse(argv=None):
                          "(context outside the measured value; an index build can use most of a run)")
     ap.add_argument("--adc-mode", type=int, default=0,
                     help="GANN_OPT_ADC_MODE: 0 auto, 1 per-query tables, 2 resident pivot table, 3 filtered")
+    ap.add_argument("--order", default="input", choices=["input", "partition"],
+                    help="record order of the built index: as generated, or grouped by coarse partition")
+    ap.add_argument("--layout", type=int, default=0,
+                    help="gann_config.layout: 0 auto (neighbour-code block when it fits), 1 without it, 2 with it")
     ap.add_argument("--split-records", action="store_true",
                     help="N>1: each rank holds 1/N of the node records and reads the others over NVLink")
     ap.add_argument("--no-split-extra", action="store_true",
@@ -89,6 +94,9 @@ def parse(argv=None):
     d = DEFAULTS[a.config]
     a.nq = a.nq or d["nq"]
     a.efs = a.efs or d["efs"]
+    a.topk = d.get("topk", TOPK)
+    from gustann_b200.index.make import PARAMS
+    a.pq_chunks, a.metric = PARAMS[a.config]["M"], PARAMS[a.config]["metric"]
     return a
 
 
@@ -255,7 +263,8 @@ def traffic_per_launch(cfg_key: str, n: int, ef: int, hops: int):
 
 # ------------------------------------------------------------------ data
 def index_root(args, spec) -> str:
-    return os.path.join(args.cache, f"{args.config}_n{spec.n}_q{args.nq}_v4")
+    tag = "" if args.order == "input" else f"_{args.order}"
+    return os.path.join(args.cache, f"{args.config}_n{spec.n}_q{args.nq}_v4{tag}")
 
 
 def passes_for(args, spec) -> int:
@@ -270,7 +279,7 @@ def ensure_index(args, spec, d: Dist) -> str:
     if d.rank == 0 and not os.path.exists(done):
         cmd = [sys.executable, "-m", "gustann_b200.index.make", "--config", args.config, "--root", root,
                "--points", str(spec.n), "--nq", str(args.nq), "--passes", str(passes_for(args, spec)),
-               "--device", str(d.local)]
+               "--device", str(d.local), "--order", args.order]
         r = subprocess.run(cmd, cwd=ROOT, stdout=sys.stderr, stderr=sys.stderr)
         if r.returncode != 0 or not os.path.exists(done):
             raise RuntimeError(f"index build failed (rc={r.returncode}): {' '.join(cmd)}")
@@ -311,11 +320,14 @@ def recall_at(nns: np.ndarray, gt: np.ndarray, k: int = TOPK) -> float:
 
 
 def config_json(args, spec, ef, rec, passes):
+    qdist = (f"Zipf({spec.zipf:g})-skewed over the centers, noise sigma {spec.query_noise:g}" if spec.zipf
+             else "from the same mixture")
     return {"workload": f"{args.config}: {spec.n} x {spec.dim}-d {'uint8' if spec.dtype == 0 else 'float32'} "
                         f"{spec.kind}-like mixture ({spec.centers} centers, sigma {spec.sigma:g}), Vamana R=64 "
-                        f"alpha=1.2 ({passes} pass{'es' if passes > 1 else ''}), PQ M=32, pivot graph (1M samples), "
-                        f"{args.nq} queries sharded over the ranks, top-{TOPK}, L2",
-            "ef_search": ef, "recall_at_10": rec, "recall_target": args.target, "queries_total": args.nq,
+                        f"alpha=1.2 ({passes} pass{'es' if passes > 1 else ''}), PQ M={args.pq_chunks}, pivot graph "
+                        f"(1M samples), {args.nq} queries {qdist} sharded over the ranks, top-{args.topk}, "
+                        f"{'inner product' if args.metric else 'L2'}",
+            "ef_search": ef, f"recall_at_{args.topk}": rec, "recall_target": args.target, "queries_total": args.nq,
             "l2_flush": "not needed: index larger than L2",
             "parallelism": f"query shards x{args.gpus}, index replicated" + (
                 f", records split x{args.gpus}" if getattr(args, "split_records", False) and args.gpus > 1 else "")}
@@ -329,7 +341,7 @@ def oracle_module():
     return orc
 
 
-def cpu_baseline(o, Q, ef, seconds):
+def cpu_baseline(o, Q, ef, seconds, topk=TOPK):
     """The oracle (C restatement of the reference path) on the host cores,
     on a bounded sample of the workload's queries."""
     cores = os.cpu_count() or 1
@@ -338,7 +350,7 @@ def cpu_baseline(o, Q, ef, seconds):
     while t_total < seconds and done < 3 * len(Q):
         qb = Q[i % len(Q): i % len(Q) + batch]
         t0 = time.perf_counter()
-        o.search(qb, TOPK, ef, threads=cores)
+        o.search(qb, topk, ef, threads=cores)
         t_total += time.perf_counter() - t0
         done += len(qb)
         i += len(qb)
@@ -366,15 +378,17 @@ def run_reference(args, d: Dist):
     rq = min(len(Q), RECALL_QUERIES)
     orc = oracle_module()
     t0 = time.time()
-    o = orc.Oracle(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], spec.dtype)
+    o = orc.Oracle(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], spec.dtype,
+                   metric=args.metric)
     t_open = time.time() - t0
     cores = os.cpu_count() or 1
+    k = args.topk
     efs = [int(x) for x in args.efs.split(",")]
     ef, rec = efs[-1], 0.0
     sweep, flags_at = [], {}
     for e in efs:
-        nns, _, _, _, fl = o.search(Q[:rq], TOPK, e, threads=cores)
-        r = recall_at(nns, gt[:rq])
+        nns, _, _, _, fl = o.search(Q[:rq], k, e, threads=cores)
+        r = recall_at(nns, gt[:rq], k)
         sweep.append((e, round(r, 5)))
         flags_at[e] = fl
         if r >= args.target:
@@ -383,12 +397,12 @@ def run_reference(args, d: Dist):
         rec = r
     per_step = min(len(Q), 2000)
     for _ in range(args.warmup):
-        o.search(Q[:min(per_step, 256)], TOPK, ef, threads=cores)
+        o.search(Q[:min(per_step, 256)], k, ef, threads=cores)
     times = []
     for s_ in range(args.steps):
         qb = Q[(s_ * per_step) % len(Q):][:per_step]
         t0 = time.perf_counter()
-        o.search(qb, TOPK, ef, threads=cores)
+        o.search(qb, k, ef, threads=cores)
         times.append((time.perf_counter() - t0, len(qb)))
     o.close()
     tot_t = sum(t for t, _ in times)
@@ -396,7 +410,9 @@ def run_reference(args, d: Dist):
     v = tot_q / tot_t
     ref_gpu = None
     elapsed = time.time() - T_START
-    if orc.RefGPU.available() and not args.no_reference_gpu and elapsed > args.context_budget:
+    if args.metric != 0:
+        ref_gpu = {"skipped": "the reference has no inner-product search"}
+    elif orc.RefGPU.available() and not args.no_reference_gpu and elapsed > args.context_budget:
         ref_gpu = {"skipped": f"the run had used {elapsed:.0f} s (index build included) before this optional step"}
     elif orc.RefGPU.available() and not args.no_reference_gpu:
         t0 = time.time()
@@ -405,12 +421,12 @@ def run_reference(args, d: Dist):
         rsweep, keep = [], {}
         for e, _ in sweep:
             clean = np.nonzero(flags_at[e] == 0)[0]
-            rn, rd, rf, _ = r.search(Q[clean], TOPK, e)
-            rsweep.append((e, round(recall_at(rn, gt[clean]), 5), int(len(clean))))
+            rn, rd, rf, _ = r.search(Q[clean], k, e)
+            rsweep.append((e, round(recall_at(rn, gt[clean], k), 5), int(len(clean))))
             keep[e] = (clean, rn, rd, rf)
         clean, rn, rd, rf = keep[ef]
-        r.search(Q[clean], TOPK, ef)
-        rts = [r.search(Q[clean], TOPK, ef)[3] for _ in range(args.steps)]
+        r.search(Q[clean], k, ef)
+        rts = [r.search(Q[clean], k, ef)[3] for _ in range(args.steps)]
         r.close()
         np.savez(os.path.join(root, f"refgpu_ef{ef}.npz"), idx=clean, nns=rn, dist=rd, found=rf)
         ref_gpu = {"value": len(clean) / float(np.mean(rts)), "unit": "queries/s", "ef_search": ef,
@@ -437,7 +453,7 @@ def parity_report(args, o, root, Qs, nns, dist, found, ef):
     first `parity_queries` queries, and against the reference's own kernels
     (results the reference arm left in the cache) on every query they ran."""
     n = min(args.parity_queries, len(Qs))
-    onns, odist, ofound, _, fl = o.search(Qs[:n], TOPK, ef, threads=os.cpu_count() or 1)
+    onns, odist, ofound, _, fl = o.search(Qs[:n], args.topk, ef, threads=os.cpu_count() or 1)
     out = {"oracle": {"queries": n, "id_mismatches": int((onns != nns[:n]).any(1).sum()),
                       "dist_mismatches": int((odist != dist[:n]).any(1).sum()),
                       "found_mismatches": int((ofound != found[:n]).sum()),
@@ -464,7 +480,8 @@ def run_ours(args, d: Dist):
     dev = d.local
     lo, hi = shard(len(Q), d.rank, d.world)
     Qs = np.ascontiguousarray(Q[lo:hi])
-    g = GustANN(spec.dtype, device=dev)
+    g = GustANN(spec.dtype, device=dev, layout=args.layout, metric=args.metric)
+    k = args.topk
     cfg = GustANNConfig(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"])
     t0 = time.time()
     split = args.split_records and d.world > 1
@@ -485,27 +502,27 @@ def run_ours(args, d: Dist):
     efs = [int(x) for x in args.efs.split(",")]
     sweep, ef = [], None
     for e in efs:
-        nns, _, _ = g.query(Q[:rq], TOPK, e)
-        r = recall_at(nns, gt[:rq])
+        nns, _, _ = g.query(Q[:rq], k, e)
+        r = recall_at(nns, gt[:rq], k)
         sweep.append((e, round(r, 5)))
         if ef is None and r >= args.target:
             ef = e
     ef = int(d.max(float(ef if ef is not None else efs[-1])))
     st = GustANNStats()
-    nns, dist, found = g.query(Qs, TOPK, ef, st)
+    nns, dist, found = g.query(Qs, k, ef, st)
     assert st.capped_queries == 0
-    hits = d.sum(float(recall_hits(nns, gt[lo:hi])))
-    rec = hits / (len(Q) * TOPK)
+    hits = d.sum(float(recall_hits(nns, gt[lo:hi], k)))
+    rec = hits / (len(Q) * k)
 
     nq = len(Qs)
     dq = torch.from_numpy(Qs).cuda(dev)
-    dn = torch.empty((nq, TOPK), dtype=torch.int32, device=dev)
-    dd = torch.empty((nq, TOPK), dtype=torch.float32, device=dev)
+    dn = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    dd = torch.empty((nq, k), dtype=torch.float32, device=dev)
     df = torch.empty(nq, dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)
 
     def launch():
-        g.search_device(dq.data_ptr(), nq, TOPK, ef, dn.data_ptr(), dd.data_ptr(), df.data_ptr(), 0,
+        g.search_device(dq.data_ptr(), nq, k, ef, dn.data_ptr(), dd.data_ptr(), df.data_ptr(), 0,
                         stream.cuda_stream)
 
     for _ in range(args.warmup):
@@ -535,16 +552,16 @@ def run_ours(args, d: Dist):
 
     # e2e: the reference-facing call with host buffers (pinned), copies included
     hq = torch.from_numpy(Qs).pin_memory().numpy()
-    hn = torch.zeros((nq, TOPK), dtype=torch.int32).pin_memory().numpy()
-    hd = torch.zeros((nq, TOPK), dtype=torch.float32).pin_memory().numpy()
+    hn = torch.zeros((nq, k), dtype=torch.int32).pin_memory().numpy()
+    hd = torch.zeros((nq, k), dtype=torch.float32).pin_memory().numpy()
     hf = torch.zeros(nq, dtype=torch.int32).pin_memory().numpy()
     for _ in range(args.warmup):
-        g.search(hq, nq, TOPK, ef, hn, hd, hf)
+        g.search(hq, nq, k, ef, hn, hd, hf)
     d.barrier()
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        g.search(hq, nq, TOPK, ef, hn, hd, hf)
+        g.search(hq, nq, k, ef, hn, hd, hf)
     t_e2e = (time.perf_counter() - t0) / args.steps
     d.barrier()
     t_e2e = d.max(t_e2e)
@@ -565,7 +582,7 @@ def run_ours(args, d: Dist):
     split_extra = None
     if d.world > 1 and not split and not args.no_split_extra:
         from gustann_b200.sharding import exchange_parts
-        gs = GustANN(spec.dtype, device=dev)
+        gs = GustANN(spec.dtype, device=dev, metric=args.metric)
         gs.init_pure_mem(cfg, True, part_count=d.world, part_index=d.rank)
         if args.adc_mode:
             from gustann_b200.api import GANN_OPT_ADC_MODE
@@ -573,7 +590,7 @@ def run_ours(args, d: Dist):
         exchange_parts(gs, d.rank, d.world)
 
         def launch_split():
-            gs.search_device(dq.data_ptr(), nq, TOPK, ef, dn.data_ptr(), dd.data_ptr(), df.data_ptr(), 0,
+            gs.search_device(dq.data_ptr(), nq, k, ef, dn.data_ptr(), dd.data_ptr(), df.data_ptr(), 0,
                              stream.cuda_stream)
 
         for _ in range(args.warmup):
@@ -602,9 +619,10 @@ def run_ours(args, d: Dist):
         cpu = parity = None
         if d.world == 1 and not args.no_cpu_baseline:
             orc = oracle_module()
-            o = orc.Oracle(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], spec.dtype)
+            o = orc.Oracle(paths["index_file"], paths["pq_file_prefix"], paths["nav_graph_prefix"], spec.dtype,
+                           metric=args.metric)
             parity = parity_report(args, o, root, Qs, nns, dist, found, ef)
-            cpu = cpu_baseline(o, Qs[:rq], ef, args.cpu_seconds)
+            cpu = cpu_baseline(o, Qs[:rq], ef, args.cpu_seconds, k)
             o.close()
         ref_sweep = None
         p = os.path.join(root, "reference_sweep.json")
@@ -619,7 +637,7 @@ def run_ours(args, d: Dist):
                "roofline": roof, "cpu_baseline": cpu, "clocks": ck, "gpu_launches": args.steps,
                "parity": parity, "timed_results_equal_untimed": same, "recall_sweep": table,
                "index_build_s": meta.get("timings"), "index_load_s": round(t_open, 1),
-               "adc_mode": args.adc_mode, "split_records": split_extra}
+               "adc_mode": args.adc_mode, "layout": args.layout, "split_records": split_extra}
     d.barrier()          # split records: peers read this rank's range until every rank is done
     g.close()
     return out

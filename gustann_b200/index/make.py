@@ -58,7 +58,7 @@ def ground_truth(X: torch.Tensor, Q: torch.Tensor, k: int, metric: int, block: i
 
 
 def make(config: str, root: str, n: int = 0, nq: int = 10_000, passes: int = 2, nav_samples: int = 1_000_000,
-         verbose: bool = True) -> dict:
+         verbose: bool = True, order: str = "input") -> dict:
     spec = datagen.CONFIGS[config]
     spec = dataclasses.replace(spec, n=n or spec.n)
     p = PARAMS[config]
@@ -68,6 +68,18 @@ def make(config: str, root: str, n: int = 0, nq: int = 10_000, passes: int = 2, 
     X = datagen.base_vectors(spec, device="cuda")
     torch.cuda.synchronize()
     t["datagen_s"] = time.time() - t0
+    if order == "partition":
+        # rows grouped by coarse partition (reorder.py); ids.bin maps each
+        # index row to its generated row, and the ground truth and search
+        # results both use index rows
+        from .reorder import partition_order
+        t0 = time.time()
+        perm = partition_order(X)
+        X = X[perm]
+        perm.to(torch.int32).cpu().numpy().tofile(os.path.join(root, "ids.bin"))
+        del perm
+        torch.cuda.synchronize()
+        t["order_s"] = time.time() - t0
     paths = pipeline.build_index(root, X, spec.dtype, R=p["R"], alpha=1.2, M=p["M"], nav_samples=nav_samples,
                                  passes=passes, verbose=verbose)
     t.update(paths["meta"]["timings"])
@@ -78,7 +90,7 @@ def make(config: str, root: str, n: int = 0, nq: int = 10_000, passes: int = 2, 
     formats.write_vecs(os.path.join(root, "gt.ivecs"), gt.astype(np.int32))
     torch.cuda.synchronize()
     t["gt_s"] = time.time() - t0
-    meta = dict(paths["meta"], config=config, nq=nq, gt_k=p["k"], metric=p["metric"], passes=passes,
+    meta = dict(paths["meta"], config=config, nq=nq, gt_k=p["k"], metric=p["metric"], passes=passes, order=order,
                 spec=dataclasses.asdict(spec), timings=t)
     with open(os.path.join(root, "meta.json"), "w") as f:
         json.dump(meta, f)
@@ -98,9 +110,11 @@ def main():
     ap.add_argument("--passes", type=int, default=2)
     ap.add_argument("--nav-samples", type=int, default=1_000_000)
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--order", default="input", choices=["input", "partition"],
+                    help="record order: as generated, or grouped by coarse partition (reorder.py)")
     a = ap.parse_args()
     torch.cuda.set_device(a.device)
-    make(a.config, a.root, a.points, a.nq, a.passes, a.nav_samples)
+    make(a.config, a.root, a.points, a.nq, a.passes, a.nav_samples, order=a.order)
 
 
 if __name__ == "__main__":

@@ -58,6 +58,16 @@ def test_defaults_name_the_headline_configuration():
     assert a.config == "c2" and a.nq == 100_000
     efs = [int(x) for x in a.efs.split(",")]
     assert efs == sorted(efs)
+    assert (a.topk, a.pq_chunks, a.metric) == (10, 32, 0)
+
+
+def test_configuration_4_is_inner_product_top_100():
+    a = bench.parse(["--config", "c4"])
+    assert (a.topk, a.pq_chunks, a.metric) == (100, 96, 1)
+    efs = [int(x) for x in a.efs.split(",")]
+    assert efs == sorted(efs) and efs[0] >= a.topk
+    c = bench.config_json(a, bench.spec_for(a), efs[0], 0.9, 2)
+    assert "recall_at_100" in c and "inner product" in c["workload"] and "Zipf(1.1)" in c["workload"]
 
 
 def test_clock_samples_inside_the_window():
