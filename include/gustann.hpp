@@ -6,6 +6,7 @@
 #pragma once
 
 #include <chrono>
+#include <future>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -38,9 +39,10 @@ struct GustANNStats {
   long long bytes_touched = 0;
 };
 
-// src/hybrid_config.hpp:8-19. mini_batch (> 0: queries per hop batch) and
-// thread_cnt (page reader threads) are used; the IO backend is always a
-// threaded pread of the local index file (src/io/mem_io.cpp's role).
+// src/hybrid_config.hpp:8-19. mini_batch (> 0: queries per hop batch),
+// thread_cnt (page reader threads) and ctx_per_thread (mini-batches in flight,
+// whose page reads overlap each other's GPU hops) are used; the IO backend is
+// always a threaded pread of the local index file (src/io/mem_io.cpp's role).
 struct HybridExecutorConfig {
   int mini_batch = 0;
   int thread_cnt = 0;
@@ -116,35 +118,93 @@ class GustANN {
   gann_handle* handle() const { return h_; }
 
  private:
+  // Mini-batches of `mini_batch` queries, `ctx_per_thread` of them in flight
+  // (src/hybrid.cu:56-58,82-83: contexts per reader thread). With one, each
+  // round reads the pages of the batch's next nodes, then runs its hop. With
+  // K >= 2 the batches take turns: while batch i's hop runs on the GPU, a
+  // second host thread reads the pages batch i+1 (mod K) asked for, so page
+  // reads and GPU steps overlap. Every batch is independent, so results do
+  // not depend on K.
+  struct HopSlot {
+    gann_hop_batch* b = nullptr;
+    int lo = 0, n = 0;
+    int64_t active = 0;
+    std::vector<int32_t> ids;
+    std::vector<unsigned char> pages;
+  };
+
   void search_hybrid(const float* qdata, int nq, int topk, int ef, int* nns, float* distances, int* found_cnt,
                      GustANNStats* stats) {
     const auto t0 = std::chrono::steady_clock::now();
     gann_info info{};
     check(gann_index_info(h_, &info));
     const int batch = hybrid_.mini_batch > 0 ? hybrid_.mini_batch : (nq > 0 ? nq : 1);
-    std::vector<int32_t> ids;
-    std::vector<unsigned char> pages;
+    const int k = hybrid_.ctx_per_thread > 1 ? hybrid_.ctx_per_thread : 1;
+    std::vector<HopSlot> slot(static_cast<size_t>(k));
+    int next = 0;
     long long hops = 0;
-    for (int lo = 0; lo < nq; lo += batch) {
-      const int n = nq - lo < batch ? nq - lo : batch;
-      gann_hop_batch* b = nullptr;
-      check(gann_hop_begin(h_, qdata + static_cast<size_t>(lo) * info.dim, n, topk, ef, &b));
-      ids.assign(n, -1);
-      pages.assign(static_cast<size_t>(n) * 4096, 0);
+    // the next mini-batch into slot s, with its entry nodes requested
+    auto open = [&](HopSlot& s) -> int {
+      s.b = nullptr;
+      s.active = 0;
+      if (next >= nq) return GANN_OK;
+      s.lo = next;
+      s.n = nq - next < batch ? nq - next : batch;
+      next += s.n;
+      int rc = gann_hop_begin(h_, qdata + static_cast<size_t>(s.lo) * info.dim, s.n, topk, ef, &s.b);
+      if (rc != GANN_OK) return rc;
+      s.ids.assign(static_cast<size_t>(s.n), -1);
+      s.pages.assign(static_cast<size_t>(s.n) * 4096, 0);
+      return gann_hop_requests(s.b, s.ids.data(), &s.active);
+    };
+    auto read = [&](HopSlot& s) -> int {
+      return s.b && s.active ? gann_read_pages(index_file_.c_str(), s.ids.data(), s.n, info.nodes_per_page,
+                                               s.pages.data(), hybrid_.thread_cnt)
+                             : GANN_OK;
+    };
+    // one hop of slot s (its pages already read); a finished batch writes its
+    // results and the slot takes the next one
+    auto step = [&](HopSlot& s) -> int {
+      if (!s.b) return GANN_OK;
       int rc = GANN_OK;
-      for (;;) {
-        int64_t active = 0;
-        if ((rc = gann_hop_requests(b, ids.data(), &active)) != GANN_OK || active == 0) break;
-        if ((rc = gann_read_pages(index_file_.c_str(), ids.data(), n, info.nodes_per_page, pages.data(),
-                                  hybrid_.thread_cnt)) != GANN_OK) break;
-        if ((rc = gann_hop_step(b, pages.data())) != GANN_OK) break;
+      if (s.active) {
+        if ((rc = gann_hop_step(s.b, s.pages.data())) != GANN_OK) return rc;
         ++hops;
+        if ((rc = gann_hop_requests(s.b, s.ids.data(), &s.active)) != GANN_OK) return rc;
       }
-      if (rc == GANN_OK)
-        rc = gann_hop_finish(b, nns + static_cast<size_t>(lo) * topk, distances + static_cast<size_t>(lo) * topk,
-                             found_cnt + lo);
-      gann_hop_free(b);
+      if (s.active) return GANN_OK;
+      rc = gann_hop_finish(s.b, nns + static_cast<size_t>(s.lo) * topk, distances + static_cast<size_t>(s.lo) * topk,
+                           found_cnt + s.lo);
+      gann_hop_free(s.b);
+      s.b = nullptr;
+      return rc != GANN_OK ? rc : open(s);
+    };
+    auto any_open = [&]() {
+      for (const HopSlot& s : slot)
+        if (s.b) return true;
+      return false;
+    };
+    auto fail = [&](int rc) {
+      for (HopSlot& s : slot)
+        if (s.b) gann_hop_free(s.b);
       check(rc);
+    };
+    int rc = GANN_OK;
+    for (HopSlot& s : slot)
+      if ((rc = open(s)) != GANN_OK) fail(rc);
+    if (k == 1) {
+      while (slot[0].b) {
+        if ((rc = read(slot[0])) != GANN_OK || (rc = step(slot[0])) != GANN_OK) fail(rc);
+      }
+    } else {
+      if ((rc = read(slot[0])) != GANN_OK) fail(rc);
+      for (int cur = 0; any_open(); cur = (cur + 1) % k) {
+        HopSlot& nx = slot[static_cast<size_t>((cur + 1) % k)];
+        std::future<int> pending = std::async(std::launch::async, [&]() { return read(nx); });
+        const int rs = step(slot[static_cast<size_t>(cur)]);
+        const int rr = pending.get();
+        if (rs != GANN_OK || rr != GANN_OK) fail(rs != GANN_OK ? rs : rr);
+      }
     }
     if (stats) {
       *stats = GustANNStats();
@@ -154,7 +214,6 @@ class GustANN {
       stats->hops = hops;   // hop rounds (one page read per active query each)
     }
   }
-
 
   static void check(int rc) {
     if (rc != GANN_OK) throw std::runtime_error(std::string("gann error ") + std::to_string(rc) + ": " + gann_last_error());
