@@ -53,7 +53,8 @@ DEFAULTS = {
                               "384,448,512,640,768,1024"),
     "c2": dict(nq=100_000, efs="32,48,64,96,128,160,192,224,256,288,320,336,352,368,384,400,416,432,448,464,"
                                "480,496,512,576,640,768,1024"),
-    "c4": dict(nq=10_000, topk=100, efs="100,112,128,144,160,176,192,224,256,288,320,384,448,512,640,768,1024"),
+    "c4": dict(nq=10_000, topk=100, efs="100,128,160,192,224,256,320,384,448,512,576,640,704,768,800,832,864,"
+                                        "896,960,1024,1280"),
 }
 RECALL_QUERIES = 10_000   # queries whose recall chooses the operating point (the first of the set)
 T_START = time.time()
