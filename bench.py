@@ -51,8 +51,8 @@ DEFAULTS = {
     "c0": dict(nq=10_000, efs="20,24,28,32,40,48,56,64,80,96,112,128,160,192,256"),
     "c1": dict(nq=10_000, efs="32,48,64,80,96,112,128,136,144,152,160,168,176,184,192,200,208,224,240,256,288,320,"
                               "384,448,512,640,768,1024"),
-    "c2": dict(nq=100_000, efs="32,48,64,96,128,160,192,224,256,288,320,336,352,368,384,400,416,432,448,464,"
-                               "480,496,512,576,640,768,1024"),
+    "c2": dict(nq=100_000, efs="32,48,64,96,128,160,192,224,256,288,320,336,352,368,376,384,392,400,408,416,"
+                               "432,448,464,480,496,512,576,640,768,1024"),
     "c4": dict(nq=10_000, topk=100, efs="100,128,160,192,224,256,320,384,448,512,576,640,704,768,800,832,864,"
                                         "896,960,1024,1280"),
 }
