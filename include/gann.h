@@ -203,9 +203,10 @@ int gann_open_device(const gann_device_index* desc, gann_handle** out);
  * 2048*dim + 4096*pq_chunks bytes; an index needing more than the array is
  * rejected with GANN_EUNSUPPORTED. The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress) and keeps it for the life of
- * the process. The address
- * belongs to the device's primary context: call from that context, and a
- * cudaDeviceReset ends the array's use by this entry point for the process.
+ * the process; that first call on a device should come before any stream
+ * capture. The address belongs to the device's primary context: call from
+ * that context, and a cudaDeviceReset ends the array's use by this entry
+ * point for the process.
  * All calls share the one array and each call re-stages it, so calls whose
  * work overlaps on the GPU race: serialise them (one stream, or wait for the
  * previous call). Asynchronous on `stream`: desc's host arrays (pivots,
