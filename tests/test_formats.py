@@ -47,7 +47,7 @@ def test_disk_index_round_trip(tmp_path, dtype, dim, R):
     assert np.array_equal(nb2[m], adj[m])
 
 
-def test_record_geometry_matches_survey_table():
+def test_record_geometry_of_the_five_configurations():
     # node_len / nodes per page of the five configurations
     assert formats.record_geometry(128, 1, 64) == (388, 10)
     assert formats.record_geometry(96, 4, 64) == (644, 6)
