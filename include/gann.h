@@ -256,7 +256,10 @@ int gann_part_attach(gann_handle* h, int32_t part, const void* blob, int64_t blo
  *   gann_hop_finish    results, as gann_search writes them
  *   gann_hop_free      release the batch (the handle stays open)
  * Needs dim * element size and the record length to be multiples of 4 bytes.
- * The handle must outlive its batches and is not used by other calls meanwhile.
+ * The handle must outlive its batches. Several batches of one handle may be
+ * open at once (each holds its own device state); calls on a handle and its
+ * batches must not run concurrently from several threads (gann_read_pages,
+ * which takes no handle, may).
  */
 typedef struct gann_hop_batch gann_hop_batch;
 int gann_hop_begin(gann_handle* h, const float* queries, int64_t nq, int32_t topk, int32_t ef_search,
