@@ -233,6 +233,17 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
+def bytes_moved_32(dim: int, elem: int, degree: int, chunks: int, nq: int, topk: int, hops: int, adc: int) -> int:
+    """The algorithmic bytes rounded to 32-byte sectors, per launch: each
+    query's float32 row, per hop the node's vector (dim x elem) and its whole
+    adjacency row (degree slots of 4 B, padding included, as the kernel reads
+    it), one code row per neighbour, and the top-k ids and distances written."""
+    def r32(b):
+        return -(-b // 32) * 32
+    return (nq * r32(4 * dim) + hops * (r32(dim * elem) + r32(4 * degree)) + adc * r32(chunks)
+            + nq * topk * 8)
+
+
 def traffic_per_launch(cfg_key: str, n: int, ef: int, hops: int):
     """DRAM bytes (read + write) per launch of the search kernel, from a
     committed ncu summary under profiles/ that names this configuration: a line
@@ -577,6 +588,9 @@ def run_ours(args, d: Dist):
             "peak_kind": peak_kind,
             "algorithmic_bytes_per_launch": int(st.bytes_touched),
             "hops_per_query": st.hops / nq, "adc_per_query": st.adc_evals / nq}
+    inf = g.info()
+    roof["bytes_moved_32b_per_launch"] = bytes_moved_32(inf["dim"], 1 if spec.dtype == 0 else 4, inf["max_degree"],
+                                                        inf["pq_chunks"], nq, k, int(st.hops), int(st.adc_evals))
 
     # N > 1 and a replicated index: the same shards and ef once more with the
     # records split over the ranks (configuration 3's layout), as an extra key

@@ -95,3 +95,11 @@ def test_clock_samples_inside_the_window():
     c.lines = [(0.5, row.format(mhz=1500, cap="Not Active")), (3.0, row.format(mhz=1600, cap="Not Active"))]
     r = c.stop(1.0, 1.001)
     assert r["samples"] == 2 and r["window"].startswith("nearest")
+
+
+def test_sector_rounded_bytes():
+    # c2 shape: 128-d uint8, 64 slots, 32 chunks; one query, 2 hops, 100 neighbours
+    b = bench.bytes_moved_32(128, 1, 64, 32, 1, 10, 2, 100)
+    assert b == 512 + 2 * (128 + 256) + 100 * 32 + 80
+    # c1 shape: 96-d float32 (384 B rows), odd sizes round up
+    assert bench.bytes_moved_32(96, 4, 61, 30, 1, 1, 1, 1) == 384 + 384 + 256 + 32 + 8
