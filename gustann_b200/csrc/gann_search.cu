@@ -616,6 +616,8 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
   float xv[VP];
   load_node<T, NPL, VP>(ix, u, lane, nb, xv);
   __syncwarp();
+  int ppos = -1;            // the pool is empty before the first hop
+  uint64_t pstar = ~0ull;
 
   for (;;) {
     if (hops >= static_cast<uint32_t>(a.max_hops)) {
@@ -663,18 +665,8 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     }
     __syncwarp();
 
-    // first unvisited pool entry; every entry before `pfirst` is visited
-    int ppos = -1;
-    for (int j = pfirst >> 5; kWarp * j < psize; ++j) {
-      const int i = lane + kWarp * j;
-      const unsigned bm = __ballot_sync(kFull, i < psize && (s.pool[i] & 1ull));
-      if (bm) {
-        ppos = kWarp * j + __ffs(bm) - 1;
-        break;
-      }
-    }
-    pfirst = ppos >= 0 ? ppos : psize;
-    const uint64_t pstar = ppos >= 0 ? s.pool[ppos] : ~0ull;
+    // pstar = the first unvisited pool entry, at ppos (found at the end of
+    // the previous hop)
 
     // ADC of every neighbour not known to be in the pool, chunks in order
     float dsum[NPL];
@@ -996,6 +988,21 @@ __device__ void traverse(const DeviceIndex& ix, const SearchArgs& a, int64_t qid
     for (int k = 0; k < NPL; ++k) nb[k] = nb2[k];
 #pragma unroll
     for (int v = 0; v < VP; ++v) xv[v] = xv2[v];
+
+    // first unvisited pool entry for the next hop (every entry before
+    // `pfirst` is visited); scanned here, while the next node's record loads
+    // are in flight, rather than after the next hop's visited-table reads
+    ppos = -1;
+    for (int j = pfirst >> 5; kWarp * j < psize; ++j) {
+      const int i = lane + kWarp * j;
+      const unsigned bm = __ballot_sync(kFull, i < psize && (s.pool[i] & 1ull));
+      if (bm) {
+        ppos = kWarp * j + __ffs(bm) - 1;
+        break;
+      }
+    }
+    pfirst = ppos >= 0 ? ppos : psize;
+    pstar = ppos >= 0 ? s.pool[ppos] : ~0ull;
   }
 
   int32_t* nns = a.nns + qid * topk;
